@@ -1,0 +1,165 @@
+/*
+ * C ABI of librecap_b200.so: the corrected sparse attention operator of RECAP on
+ * NVIDIA B200 (sm_100a).
+ *
+ * Conventions
+ *  - All pointers are device pointers unless stated otherwise; sizes are element counts.
+ *  - bf16 tensors are passed as `void*`, fp16 ones as `void*`, fp32 as `float*`.
+ *  - A "bank" is one (batch, head) pair: banks = batch * heads, bank = b * heads + h.
+ *  - Geometry derived from (S, n_video) with 128-token blocks:
+ *        NB = ceil(S/128), S_pad = 128*NB, nB = ceil(n_video/128),
+ *        nB_pad = 128*ceil(nB/128), rows = 128*floor(n_video/128),
+ *        dense_start = nB-1 if (n_video % 128 and S > n_video) else nB.
+ *  - "Reordered" means the token order [Hilbert-ordered video | text] of
+ *    recap/sparse/layout.py; "native" is the model's own order.
+ *  - Every entry point returns 0 on success or a RECAP_ERR_* code.  Nothing
+ *    synchronises the stream or allocates device memory; scratch buffers come
+ *    from the caller.  Kernels that wait on on-chip barriers give up after a
+ *    bounded time and record RECAP_STATUS_* in the caller's `status` word
+ *    (device int, zero-initialised), which the caller reads after the stream.
+ *  - The stream is a cudaStream_t passed as `void*` (NULL = legacy default stream).
+ */
+#ifndef RECAP_B200_H_
+#define RECAP_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RECAP_B200_ABI_VERSION 1
+
+#define RECAP_OK 0
+#define RECAP_ERR_SHAPE 1
+#define RECAP_ERR_LAUNCH 2
+#define RECAP_ERR_DEVICE 3
+#define RECAP_ERR_UNSUPPORTED 4
+
+/* values of the device status word */
+#define RECAP_STATUS_TIMEOUT_TMA 101
+#define RECAP_STATUS_TIMEOUT_MMA 102
+#define RECAP_STATUS_TIMEOUT_SOFTMAX 103
+#define RECAP_STATUS_TIMEOUT_PRODUCER 104
+
+int recap_abi_version(void);
+
+/* Layout gather fused with block pooling.
+ * Replaces Layout.reorder (recap/sparse/layout.py:86-90) of Q, K and V and the
+ * pool_blocks calls (recap/sparse/pooling.py:10-34) of recap/sparse/attention.py:81-82,173-174.
+ *   q, k, v        native [batch, heads, S, D] bf16; element strides (b, h, s) of q, k, v in
+ *                  `strides[0..8]` (host array), D contiguous; q or v may be NULL
+ *   src_row        [S] int32, native token of reordered row r (Layout._gather_indices fwd)
+ *   q_reordered, k_reordered  [banks, S_pad, D] bf16 out (nullable)
+ *   v_transposed   [banks, D, S_pad] bf16 out, reordered V transposed (nullable)
+ *   q_mean, k_mean, v_mean    [banks, nB, D] fp32 block means over video tokens (nullable)
+ *   k_mean_bf16    [banks, nB_pad, D] bf16 (nullable), v_mean_t_bf16 [banks, D, nB_pad] bf16
+ *                  (nullable); their padding rows/columns must be zero. */
+int recap_layout_gather(const void* q, const void* k, const void* v, const int64_t* strides, int batch,
+                        int heads, int S, int D, int n_video, const int32_t* src_row, void* q_reordered,
+                        void* k_reordered, void* v_transposed, float* q_mean, float* k_mean,
+                        float* v_mean, void* k_mean_bf16, void* v_mean_t_bf16, void* stream);
+
+/* Top-k block selection.
+ * Replaces SparseAttention.head_partition (recap/sparse/attention.py:74-94) with
+ * block_proxy_mask (recap/sparse/router.py:10-23): score = (qbar . kbar) * scale in fp32,
+ * the `keep` highest-scoring key blocks per query block (ties: lower block index first),
+ * then the trailing partial video block selected as a row and a column.
+ *   partition      [banks, nB, nB] uint8 (bool) out */
+int recap_pool_select(const float* q_mean, const float* k_mean, int banks, int nB, int D, int keep,
+                      float scale, int n_video, int block_size, uint8_t* partition, void* stream);
+
+/* out2[0] = sum(new & old), out2[1] = sum(new) over n bytes; int64 device array.
+ * Replaces the overlap of the re-selection test, recap/operator.py:288-291 and 425-428. */
+int recap_partition_overlap(const uint8_t* new_partition, const uint8_t* old_partition, int64_t n,
+                            long long* out2, void* stream);
+
+/* Kernel block mask [banks, NB, NB] uint8 from a partition.
+ * Replaces build_kernel_block_mask (recap/kernels/block_sparse.py:52-75). */
+int recap_kernel_block_mask(const uint8_t* partition, int banks, int S, int n_video, uint8_t* mask,
+                            void* stream);
+
+/* Floats of scratch `workspace` that recap_closure_stats needs. */
+int64_t recap_closure_workspace_floats(int banks, int D, int n_video);
+
+/* Moment statistics of the coarse tail, in fp32.
+ * Replaces pooled_within_block_scatter (recap/sparse/closure.py:42-73),
+ * rotated_leaf_moments_triton (recap/kernels/closure_stats.py:192-242),
+ * pooled_cross_centered_triton_fp32 (recap/kernels/closure_stats.py:245-290) and
+ * fold_rank (recap/sparse/closure.py:96-104).
+ *   scatter        [banks, D, D] out (nullable: not computed)
+ *   cvk            [banks, D, D] out, C_vk (nullable); cvk_bf16 its bf16 copy (nullable)
+ *   basis          [banks, D, D] fp32 (nullable: no variance)
+ *   variance       [banks, nB, D] out, per-block variance in the basis, folded to `rank`
+ *                  (rank 0: not folded); variance_bf16 [banks, nB_pad, D] copy (nullable). */
+int recap_closure_stats(const void* k_reordered, const void* v_transposed, const float* k_mean, int banks,
+                        int S, int D, int n_video, int rank, const float* basis, float* scatter, float* cvk,
+                        void* cvk_bf16, float* variance, void* variance_bf16, float* workspace,
+                        void* stream);
+
+/* basis_t_bf16[b][n][k] = bf16(basis[b][k][n]): the basis cast of
+ * rotated_query_square (recap/sparse/closure.py:84-86) as a K-major MMA operand. */
+int recap_basis_prep(const float* basis, int banks, int D, void* basis_t_bf16, void* stream);
+
+/* Corrected coarse tail for the cached rows (< rows), with qsq and drift fused.
+ * Replaces SparseAttention.coarse_tail_apply (recap/sparse/attention.py:204-231),
+ * build_coarse_tail_plan (recap/sparse/planner.py:12-38), coarse_tail_attention
+ * (recap/kernels/coarse_tail.py:194-312), rotated_query_square and value_drift
+ * (recap/sparse/closure.py:84-93) and, when old_lse is given, _drift_center
+ * (recap/operator.py:148-150).
+ *   counts_log     [nB] fp32, ln(tokens of each video block)
+ *   out            [banks, rows, D] bf16: coarse output + gate * drift
+ *   lse            [banks, rows] fp32
+ *   old_lse        [banks, rows] fp32 coarse LSE of the last refresh (nullable); with it,
+ *                  center [banks] = mean(lse - old_lse) using center_partial [banks, rows/128]. */
+int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const void* cvk_bf16,
+                      const void* k_mean_bf16, const void* variance_bf16, const void* v_mean_t_bf16,
+                      const uint8_t* partition, const float* counts_log, const float* old_lse, int banks,
+                      int S, int D, int n_video, float scale, float theta, void* out, float* lse,
+                      float* center_partial, float* center, int* status, void* stream);
+
+/* Exact attention over the kept 128x128 tiles, with the natural-log LSE per row.
+ * Replaces block_sparse_exact (recap/kernels/block_sparse.py:78-139) and, with
+ * all_blocks = 1, the dense aten._scaled_dot_product_flash_attention of recap/operator.py:254-256.
+ *   out            [banks, S, D] bf16; reordered row r is written at row out_pos[r]
+ *                  (out_pos NULL: row r); lse [banks, S] fp32 likewise (nullable). */
+int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                            const uint8_t* partition, int banks, int S, int D, int n_video, int all_blocks,
+                            float scale, const int32_t* out_pos, void* out, float* lse, int* status,
+                            void* stream);
+
+/* The corrected SPARSE step: block-sparse attention with the drift-weighted merge of the coarse
+ * tail and the cached refinement fused as its epilogue, written in native order.
+ * Replaces block_sparse_exact + sparse_merge (recap/kernels/detail_cache.py:402-456) +
+ * Layout.restore (recap/sparse/layout.py:92) of Operator._sparse (recap/operator.py:478-527).
+ *   detail_value   [banks, rows, D] fp16, detail_log_mass/old_lse [banks, rows] fp32, center [banks]
+ *   out            [banks, S, D] bf16, reordered row r at row out_pos[r]. */
+int recap_sparse_step(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                      const uint8_t* partition, int banks, int S, int D, int n_video, float scale,
+                      const void* coarse_out, const float* coarse_lse, const void* detail_value,
+                      const float* detail_log_mass, const float* old_lse, const float* center,
+                      const int32_t* out_pos, void* out, int* status, void* stream);
+
+/* Number of (err^2, ref^2) float pairs of scratch `partials` recap_refresh_detail needs. */
+int recap_refresh_partials(int banks, int n_video);
+
+/* Refinement write at a dense refresh, optionally scoring the old refinement first.
+ * Replaces refresh_detail (recap/kernels/detail_cache.py:304-379).
+ *   full_o/full_lse    dense output [banks, S, D] bf16 / [banks, S] fp32, native order
+ *   head_o/head_lse    block-sparse output, reordered
+ *   coarse_out/lse     [banks, rows, D] bf16 / [banks, rows]
+ *   perm               [>= rows] int32 reordered video position -> native video index
+ *   detail_value       [banks, rows, D] fp16 in/out; detail_log_mass [banks, rows] in/out
+ *   validate           nonzero: stats[2] = (sum err^2, sum of^2) before the write
+ *   old_lse/center     drift weight of the validation (both or neither; validate only). */
+int recap_refresh_detail(const void* full_o, const float* full_lse, const void* head_o, const float* head_lse,
+                         const void* coarse_out, const float* coarse_lse, const int32_t* perm, int banks, int S,
+                         int D, int n_video, int video_offset, void* detail_value, float* detail_log_mass,
+                         int validate, const float* old_lse, const float* center, float* partials,
+                         float* stats, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RECAP_B200_H_ */

@@ -1,0 +1,410 @@
+"""Attention for the EXACT, REFRESH and SPARSE steps, on B200.
+
+Drop-in for ``recap.operator`` (recap/operator.py): the same ``Operator.build``,
+``reset``, ``banks_valid``, ``begin_step``, ``set_stream``, ``attend``,
+``drain_validation`` and ``peak_bank_bytes``, the same ``DetailBank`` fields and the same
+re-selection and validation state machine, so ``recap.session.RecapSession``, the
+controller and the model processors run on it unchanged.  Every tensor operation of a
+call runs in ``librecap_b200.so``:
+
+``EXACT``    one layout pass + the attention kernel over every key block.
+``REFRESH``  dense attention with LSE, block selection (first refresh or re-rank), the
+             block-sparse head, the coarse tail and the refinement write (scoring the old
+             refinement first when one exists).
+``SPARSE``   one layout pass, the closure statistics, the coarse tail (with the drift
+             centre) and the block-sparse attention whose epilogue merges head, coarse tail
+             and drift-weighted refinement and writes native order.
+
+Inputs are ``[batch, heads, sequence, dim]`` in the model's native token order (any
+strides with ``dim`` contiguous).  The kernels compute in bf16 with fp32 accumulation;
+other input dtypes are cast to bf16 on entry and the output is cast back.
+
+Head parallelism: with ``process_group`` set, each rank holds a slice of the heads; the
+whole-layer re-selection decision and the validation sums are all-reduced over the group,
+so every rank takes the same decision the single-GPU operator would.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from .config import OperatorConfig
+from .sparse.attention import Launches, LayerInputs, SparseAttention, SparseGeometry
+from .sparse.layout import Layout
+
+EXACT = "exact"
+REFRESH = "refresh"
+SPARSE = "sparse"
+
+
+@dataclass
+class DetailBank:
+    """One layer's cached refinement and its partition (recap/operator.py:33-59)."""
+
+    partition: torch.Tensor | None = None  # [batch, heads, query blocks, key blocks] bool
+    # refinement of the tail output and of the tail log-mass
+    value: torch.Tensor | None = None  # [banks, rows, dim] fp16
+    log_mass: torch.Tensor | None = None  # [banks, rows] fp32
+    # coarse tail log-mass at the refresh, reference for the drift weight
+    coarse_lse: torch.Tensor | None = None  # [banks, rows] fp32
+    valid: bool = False
+    refreshed_at: int = 0
+    # error of the previous refinement, measured at this refresh
+    pending_stats: torch.Tensor | None = None  # [2] fp32: (sum sq error, sum sq output)
+    pending_age: int | None = None
+    sequence_tokens: int = 0
+    n_video: int = 0
+    _mask: torch.Tensor | None = field(default=None, repr=False)
+
+    @property
+    def head_kernel_mask(self) -> torch.Tensor | None:
+        """``[banks, blocks, blocks]`` bool mask on the kernel's 128-token grid (built on
+        demand from the partition; the kernels read the partition directly)."""
+        if self.partition is None:
+            return None
+        if self._mask is None:
+            b, h, nb, _ = self.partition.shape
+            NB = (self.sequence_tokens + 127) // 128
+            mask = torch.empty(b * h, NB, NB, dtype=torch.bool, device=self.partition.device)
+            _lib.call(
+                "recap_kernel_block_mask", _lib.ptr(self.partition), b * h, self.sequence_tokens,
+                self.n_video, _lib.ptr(mask), _lib.stream_handle(mask.device),
+            )
+            self._mask = mask
+        return self._mask
+
+    def set_partition(self, partition: torch.Tensor, sequence_tokens: int, n_video: int) -> None:
+        self.partition = partition
+        self.sequence_tokens = int(sequence_tokens)
+        self.n_video = int(n_video)
+        self._mask = None
+
+    def release(self) -> None:
+        self.partition = None
+        self._mask = None
+        self.value = None
+        self.log_mass = None
+        self.coarse_lse = None
+        self.valid = False
+        self.refreshed_at = 0
+        self.pending_stats = None
+        self.pending_age = None
+
+
+@dataclass
+class Operator:
+    """Dispatches one attention call per layer and owns the detail banks."""
+
+    config: OperatorConfig
+    layout: Layout
+    #: per-layer sparse state, indexed ``[stream][layer]``
+    layers: list[list[SparseAttention]]
+    banks: list[list[DetailBank]] = field(default_factory=list)
+    kind: str = EXACT
+    step: int = 0
+    stream: int = 0
+    refreshed_layers: int = 0
+    process_group: object | None = None
+    launches: Launches = field(default_factory=Launches)
+    _status: dict = field(default_factory=dict, repr=False)
+
+    def __post_init__(self) -> None:
+        if not self.layers or isinstance(self.layers[0], SparseAttention):
+            raise TypeError("Operator.layers must be indexed [stream][layer]")
+        self.banks = [[DetailBank() for _ in row] for row in self.layers]
+        for row in self.layers:
+            for layer in row:
+                layer.launches = self.launches
+
+    @classmethod
+    def build(
+        cls,
+        config: OperatorConfig,
+        geometry: SparseGeometry,
+        *,
+        n_layers: int,
+        n_streams: int = 1,
+        process_group=None,
+    ) -> "Operator":
+        """One sparse state per (stream, layer)."""
+        if n_layers < 1 or n_streams < 1:
+            raise ValueError("n_layers and n_streams must be positive")
+        if int(getattr(config, "block_size", 128)) != 128:
+            raise ValueError("the exact block-sparse kernel requires block_size=128")
+        layers = [[SparseAttention(geometry, config) for _ in range(n_layers)] for _ in range(n_streams)]
+        return cls(config, geometry.layout, layers, process_group=process_group)
+
+    @property
+    def n_streams(self) -> int:
+        return len(self.layers)
+
+    def reset(self) -> None:
+        for row in self.banks:
+            for bank in row:
+                bank.release()
+        for row in self.layers:
+            for layer in row:
+                layer.reset()
+        self.kind = EXACT
+        self.step = 0
+        self.stream = 0
+        self.refreshed_layers = 0
+
+    @property
+    def banks_valid(self) -> bool:
+        """Whether every layer holds a refinement."""
+        return bool(self.banks) and all(bank.valid for row in self.banks for bank in row)
+
+    def begin_step(self, step: int, kind: str) -> None:
+        if kind not in (EXACT, REFRESH, SPARSE):
+            raise ValueError(f"unknown computed call kind {kind!r}")
+        self.step = int(step)
+        self.kind = kind
+        self.stream = 0
+        self.refreshed_layers = 0
+
+    def set_stream(self, stream: int) -> None:
+        if not 0 <= stream < self.n_streams:
+            raise ValueError(f"stream {stream} outside 0..{self.n_streams - 1}")
+        self.stream = int(stream)
+
+    # -- device status ---------------------------------------------------------------------
+
+    def status_word(self, device: torch.device) -> torch.Tensor:
+        key = str(device)
+        word = self._status.get(key)
+        if word is None:
+            word = torch.zeros(1, dtype=torch.int32, device=device)
+            self._status[key] = word
+        return word
+
+    def check_device_status(self) -> None:
+        """Raise if a kernel gave up waiting on an on-chip barrier (synchronises)."""
+        for word in self._status.values():
+            code = int(word.item())
+            if code:
+                word.zero_()
+                raise RuntimeError(
+                    f"a recap_b200 kernel reported a device timeout: "
+                    f"{_lib.STATUS_NAMES.get(code, code)}"
+                )
+
+    # -- dispatch --------------------------------------------------------------------------
+
+    @torch.no_grad()
+    def attend(
+        self,
+        layer_index: int,
+        query: torch.Tensor,
+        key: torch.Tensor,
+        value: torch.Tensor,
+    ) -> torch.Tensor:
+        """One attention call: ``[b, h, S, d]`` native order in, same shape/dtype out."""
+        if not (query.is_cuda and key.is_cuda and value.is_cuda):
+            raise ValueError("recap_b200.Operator runs on CUDA tensors only")
+        if query.shape != key.shape or key.shape != value.shape:
+            raise ValueError("Q/K/V shapes differ")
+        in_dtype = query.dtype
+        if in_dtype != torch.bfloat16:
+            query, key, value = (t.to(torch.bfloat16) for t in (query, key, value))
+        layer = self.layers[self.stream][layer_index]
+        bank = self.banks[self.stream][layer_index]
+        if self.kind == SPARSE:
+            out = self._sparse(layer, bank, query, key, value)
+        elif self.kind == EXACT:
+            out = self._exact(layer, query, key, value)
+        else:
+            out = self._refresh(layer, bank, query, key, value)
+        return out if in_dtype == torch.bfloat16 else out.to(in_dtype)
+
+    def _scale(self, query: torch.Tensor) -> float:
+        return 1.0 / math.sqrt(query.shape[-1])
+
+    def _dense(self, inputs: LayerInputs, scale: float, status, native: bool = True):
+        """Attention over every key block: output and LSE in native order."""
+        sh = inputs.shapes
+        dev = inputs.q.device
+        out = torch.empty(sh.batch, sh.heads, sh.S, sh.D, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(sh.banks, sh.S, dtype=torch.float32, device=dev)
+        self.launches.run(
+            "recap_block_sparse_fmha", 1,
+            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), None, sh.banks, sh.S, sh.D,
+            sh.n_video, 1, float(scale), _lib.ptr(self.layout.gather_rows(dev)) if native else None,
+            _lib.ptr(out), _lib.ptr(lse), _lib.ptr(status), _lib.stream_handle(dev),
+        )
+        return out, lse
+
+    def _head(self, inputs: LayerInputs, partition: torch.Tensor, scale: float, status):
+        """Block-sparse head: output and LSE in reordered order."""
+        sh = inputs.shapes
+        dev = inputs.q.device
+        out = torch.empty(sh.banks, sh.S, sh.D, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(sh.banks, sh.S, dtype=torch.float32, device=dev)
+        self.launches.run(
+            "recap_block_sparse_fmha", 1,
+            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(partition), sh.banks,
+            sh.S, sh.D, sh.n_video, 0, float(scale), None, _lib.ptr(out), _lib.ptr(lse), _lib.ptr(status),
+            _lib.stream_handle(dev),
+        )
+        return out, lse
+
+    @torch.no_grad()
+    def _exact(self, layer: SparseAttention, query, key, value) -> torch.Tensor:
+        inputs = layer.prepare(query, key, value, q_mean=False, means=False)
+        out, _ = self._dense(inputs, self._scale(query), self.status_word(query.device))
+        return out
+
+    # -- refresh ---------------------------------------------------------------------------
+
+    def _layer_overlap(self, new: torch.Tensor, old: torch.Tensor) -> tuple[int, int]:
+        """(kept, total) = (|new & old|, |new|) over the whole layer (all ranks)."""
+        counts = torch.empty(2, dtype=torch.int64, device=new.device)
+        self.launches.run(
+            "recap_partition_overlap", 1, _lib.ptr(new), _lib.ptr(old), new.numel(), _lib.ptr(counts),
+            _lib.stream_handle(new.device),
+        )
+        if self.process_group is not None:
+            import torch.distributed as dist
+
+            dist.all_reduce(counts, group=self.process_group)
+        kept, total = (int(x) for x in counts.cpu())
+        return kept, total
+
+    @torch.no_grad()
+    def _refresh(self, layer: SparseAttention, bank: DetailBank, query, key, value) -> torch.Tensor:
+        """Dense output; stores the refinement and measures the previous one
+        (recap/operator.py:331-473)."""
+        scale = self._scale(query)
+        dev = query.device
+        status = self.status_word(dev)
+        inputs = layer.prepare(query, key, value, q_mean=True)
+        sh = inputs.shapes
+        revalidating = bank.valid
+        if not revalidating:
+            bank.set_partition(layer.head_partition(inputs, scale), sh.S, sh.n_video)
+        full_out, full_lse = self._dense(inputs, scale, status)
+        head_o, head_lse = self._head(inputs, bank.partition, scale, status)
+        context = layer.coarse_tail_context(inputs, scale)
+        old_lse = bank.coarse_lse if revalidating else None
+        coarse, coarse_lse, center = layer.coarse_tail_apply(
+            inputs, context, bank.partition, scale, old_lse=old_lse, status=status
+        )
+        if bank.value is None or bank.value.shape != (sh.banks, sh.rows, sh.D):
+            bank.value = torch.empty(sh.banks, sh.rows, sh.D, dtype=torch.float16, device=dev)
+            bank.log_mass = torch.empty(sh.banks, sh.rows, dtype=torch.float32, device=dev)
+        stats = torch.zeros(2, dtype=torch.float32, device=dev) if revalidating else None
+        self._write_refinement(inputs, full_out, full_lse, head_o, head_lse, coarse, coarse_lse, bank,
+                               stats, old_lse, center)
+        if stats is not None:
+            bank.pending_stats = stats
+            bank.pending_age = self.step - bank.refreshed_at
+
+        if revalidating:
+            # Re-select the key blocks from the current attention; keep the old partition if
+            # the selection barely changed over the whole layer.
+            partition = layer.head_partition(inputs, scale)
+            if bank.partition is not None:
+                kept, total = self._layer_overlap(partition, bank.partition)
+                if kept / max(total, 1) >= self.config.rerank_min_overlap:
+                    bank.coarse_lse = coarse_lse.clone()
+                    bank.refreshed_at = self.step
+                    bank.valid = True
+                    self.refreshed_layers += 1
+                    return full_out
+            bank.set_partition(partition, sh.S, sh.n_video)
+            del head_o, head_lse, coarse, coarse_lse
+            head_o, head_lse = self._head(inputs, bank.partition, scale, status)
+            coarse, coarse_lse, _ = layer.coarse_tail_apply(inputs, context, bank.partition, scale, status=status)
+            self._write_refinement(inputs, full_out, full_lse, head_o, head_lse, coarse, coarse_lse, bank,
+                                   None, None, None)
+        bank.coarse_lse = coarse_lse.clone()
+        bank.refreshed_at = self.step
+        bank.valid = True
+        self.refreshed_layers += 1
+        return full_out
+
+    def _write_refinement(self, inputs, full_out, full_lse, head_o, head_lse, coarse, coarse_lse, bank,
+                          stats, old_lse, center) -> None:
+        sh = inputs.shapes
+        dev = full_out.device
+        partials = None
+        if stats is not None:
+            n = int(_lib.load().recap_refresh_partials(sh.banks, sh.n_video))
+            partials = torch.empty(max(n, 1), 2, dtype=torch.float32, device=dev)
+        self.launches.run(
+            "recap_refresh_detail", 1 + (stats is not None),
+            _lib.ptr(full_out), _lib.ptr(full_lse), _lib.ptr(head_o), _lib.ptr(head_lse), _lib.ptr(coarse),
+            _lib.ptr(coarse_lse), _lib.ptr(self.layout.video_permutation(dev, torch.int32)), sh.banks, sh.S,
+            sh.D, sh.n_video, self.layout.video_offset, _lib.ptr(bank.value), _lib.ptr(bank.log_mass),
+            1 if stats is not None else 0, _lib.ptr(old_lse), _lib.ptr(center), _lib.ptr(partials),
+            _lib.ptr(stats), _lib.stream_handle(dev),
+        )
+
+    # -- sparse ----------------------------------------------------------------------------
+
+    @torch.no_grad()
+    def _sparse(self, layer: SparseAttention, bank: DetailBank, query, key, value) -> torch.Tensor:
+        """Head computed exactly, plus coarse tail and weighted cached refinement
+        (recap/operator.py:478-527)."""
+        if not bank.valid or bank.partition is None:
+            raise RuntimeError("a sparse call was requested before an exact refresh")
+        scale = self._scale(query)
+        dev = query.device
+        status = self.status_word(dev)
+        inputs = layer.prepare(query, key, value, q_mean=False)
+        sh = inputs.shapes
+        if bank.partition.shape != (sh.batch, sh.heads, sh.nB, sh.nB):
+            raise ValueError("the cached partition does not match this call's shape")
+        context = layer.coarse_tail_context(inputs, scale)
+        coarse, coarse_lse, center = layer.coarse_tail_apply(
+            inputs, context, bank.partition, scale, old_lse=bank.coarse_lse, status=status
+        )
+        out = torch.empty(sh.batch, sh.heads, sh.S, sh.D, dtype=torch.bfloat16, device=dev)
+        self.launches.run(
+            "recap_sparse_step", 1,
+            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(bank.partition), sh.banks,
+            sh.S, sh.D, sh.n_video, float(scale), _lib.ptr(coarse), _lib.ptr(coarse_lse), _lib.ptr(bank.value),
+            _lib.ptr(bank.log_mass), _lib.ptr(bank.coarse_lse), _lib.ptr(center),
+            _lib.ptr(self.layout.gather_rows(dev)), _lib.ptr(out), _lib.ptr(status), _lib.stream_handle(dev),
+        )
+        return out
+
+    # -- the refinement error --------------------------------------------------------------
+
+    def drain_validation(self) -> tuple[int, float] | None:
+        """Relative RMS error over all layers, and the smallest refinement age
+        (recap/operator.py:531-547)."""
+        stats: list[torch.Tensor] = []
+        ages: list[int] = []
+        for row in self.banks:
+            for bank in row:
+                if bank.pending_stats is not None and bank.pending_age is not None:
+                    stats.append(bank.pending_stats)
+                    ages.append(int(bank.pending_age))
+                bank.pending_stats = None
+                bank.pending_age = None
+        self.check_device_status()
+        if not stats:
+            return None
+        total = torch.stack(stats).sum(dim=0)
+        if self.process_group is not None:
+            import torch.distributed as dist
+
+            dist.all_reduce(total, group=self.process_group)
+        numerator, denominator = (float(x) for x in total)
+        error = math.sqrt(numerator / denominator) if denominator > 0.0 else float("inf")
+        return min(ages), error
+
+    def peak_bank_bytes(self) -> int:
+        """Bytes held by the refinement."""
+        total = 0
+        for row in self.banks:
+            for bank in row:
+                for tensor in (bank.value, bank.log_mass):
+                    if tensor is not None:
+                        total += tensor.numel() * tensor.element_size()
+        return total

@@ -1,0 +1,297 @@
+"""Per-kernel parity of the CUDA path against the CPU oracle (and torch fp32 references
+for the floating-point kernels), called through the C ABI on small seeded inputs."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import recap_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _lib():
+    from recap_b200 import _lib as lib
+
+    return lib
+
+
+def _layout(nv, text, text_first, seed=0):
+    from recap_b200.sparse.layout import Layout
+
+    perm = np.random.default_rng(seed).permutation(nv)
+    return Layout.from_permutation(perm, text_tokens=text, text_first=text_first)
+
+
+def _strided_qkv(b, h, s, d, seed):
+    """bf16 [b, h, s, d] views of [b, s, h, d] storage (the models' layout)."""
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(3):
+        x = torch.randn(b, s, h, d, generator=g).to(torch.bfloat16).to(DEV)
+        out.append(x.transpose(1, 2))
+    return out
+
+
+def _run_gather(layout, q, k, v, q_mean=True):
+    from recap_b200.config import OperatorConfig
+    from recap_b200.sparse.attention import SparseAttention, SparseGeometry
+
+    geo = SparseGeometry.build(layout, 128)
+    sa = SparseAttention(geo, OperatorConfig())
+    return sa, sa.prepare(q, k, v, q_mean=q_mean)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("nv,text,text_first", [(2048, 0, False), (700, 50, True), (504, 40, False)])
+def test_layout_gather_and_pooling(d, nv, text, text_first):
+    lay = _layout(nv, text, text_first)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=1)
+    _, inp = _run_gather(lay, q, k, v)
+    torch.cuda.synchronize()
+    sh = inp.shapes
+    for src, name in ((q, "q"), (k, "k")):
+        ref = lay.reorder(src).reshape(sh.banks, sh.S, d)
+        got = getattr(inp, name)
+        assert torch.equal(got[:, : sh.S], ref), name
+        assert bool((got[:, sh.S:] == 0).all())
+    vref = lay.reorder(v).reshape(sh.banks, sh.S, d)
+    assert torch.equal(inp.v_t[:, :, : sh.S].transpose(1, 2), vref)
+    for src, mean in ((q, inp.q_mean), (k, inp.k_mean), (v, inp.v_mean)):
+        ref, _ = orc.pool_blocks(lay.reorder(src).reshape(sh.banks, sh.S, d).float().cpu(), nv)
+        assert torch.allclose(mean.cpu(), ref, atol=1e-5, rtol=1e-5)
+    kb = inp.k_mean_bf16[:, : sh.nB].float().cpu()
+    assert torch.equal(kb, inp.k_mean.cpu().to(torch.bfloat16).float())
+    vbt = inp.v_mean_t_bf16[:, :, : sh.nB].transpose(1, 2).float().cpu()
+    assert torch.equal(vbt, inp.v_mean.cpu().to(torch.bfloat16).float())
+
+
+def _selection_matches(got: torch.Tensor, scores: torch.Tensor, keep: int, forced: bool) -> tuple[bool, int]:
+    """Selected sets equal to the oracle's, except where a differing block's score ties
+    (within 4 fp32 ulp) with the k-th score of its row; the forced partial row/column of
+    recap/sparse/attention.py:88-94 must match exactly."""
+    ref = orc.topk_mask(scores, keep)
+    srt = torch.sort(scores.double(), dim=-1, descending=True).values
+    kth = srt[..., keep - 1 : keep]
+    tol = 4 * torch.finfo(torch.float32).eps * kth.abs().clamp_min(1e-30)
+    tie = (scores.double() - kth).abs() <= tol
+    if forced:
+        ref[..., -1, :] = True
+        ref[..., :, -1] = True
+        tie[..., -1, :] = False
+        tie[..., :, -1] = False
+    diff = got != ref
+    return bool((~diff | tie).all()), int(diff.sum())
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("nv,keep", [(2048, 4), (700, 2), (118800 // 16, 46)])
+def test_pool_select_topk(d, nv, keep):
+    from recap_b200 import _lib as lib
+
+    nB = (nv + 127) // 128
+    banks = 3
+    g = torch.Generator().manual_seed(nv + d)
+    qm = torch.randn(banks, nB, d, generator=g).to(DEV)
+    km = torch.randn(banks, nB, d, generator=g).to(DEV)
+    part = torch.empty(banks, nB, nB, dtype=torch.bool, device=DEV)
+    scale = 1 / math.sqrt(d)
+    lib.call("recap_pool_select", lib.ptr(qm), lib.ptr(km), banks, nB, d, keep, scale, nv, 128, lib.ptr(part),
+             lib.stream_handle(torch.device(DEV)))
+    got = part.cpu()
+    scores = orc.block_scores(qm.cpu(), km.cpu(), scale)
+    ok, n = _selection_matches(got, scores, keep, forced=bool(nv % 128))
+    assert ok, f"{n} selections differ beyond fp ties"
+    if not nv % 128:
+        assert bool((got.sum(-1) == keep).all())
+
+
+def test_pool_select_ties_take_lower_index():
+    from recap_b200 import _lib as lib
+
+    banks, nB, d, keep = 1, 8, 64, 3
+    qm = torch.zeros(banks, nB, d)
+    qm[..., 0] = 1.0
+    km = torch.zeros(banks, nB, d)
+    km[0, :, 0] = torch.tensor([0.5, 2.0, 1.0, 1.0, 1.0, 1.0, 0.0, 3.0])
+    part = torch.empty(banks, nB, nB, dtype=torch.bool, device=DEV)
+    lib.call("recap_pool_select", lib.ptr(qm.to(DEV)), lib.ptr(km.to(DEV)), banks, nB, d, keep, 1.0, nB * 128, 128,
+             lib.ptr(part), lib.stream_handle(torch.device(DEV)))
+    # scores per row: [0.5, 2, 1, 1, 1, 1, 0, 3] -> top 3 = {7, 1, 2} (block 2 wins the tie)
+    assert part[0, 0].cpu().tolist() == [False, True, True, False, False, False, False, True]
+
+
+def _fmha(q_r, k_r, v_t, part, banks, S, d, nv, all_blocks, out_pos=None, native_out=None):
+    from recap_b200 import _lib as lib
+
+    out = torch.empty(banks, S, d, dtype=torch.bfloat16, device=DEV) if native_out is None else native_out
+    lse = torch.empty(banks, S, dtype=torch.float32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    lib.call("recap_block_sparse_fmha", lib.ptr(q_r), lib.ptr(k_r), lib.ptr(v_t), lib.ptr(part), banks, S, d, nv,
+             int(all_blocks), 1 / math.sqrt(d), lib.ptr(out_pos), lib.ptr(out), lib.ptr(lse), lib.ptr(status),
+             lib.stream_handle(torch.device(DEV)))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, f"device status {int(status.item())}"
+    return out, lse
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("nv,text", [(1024, 0), (700, 50), (300, 9)])
+def test_fmha_dense_vs_torch_fp32(d, nv, text):
+    lay = _layout(nv, text, True)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=3)
+    _, inp = _run_gather(lay, q, k, v, q_mean=False)
+    sh = inp.shapes
+    out, lse = _fmha(inp.q, inp.k, inp.v_t, None, sh.banks, sh.S, d, nv, True)
+    qr = inp.q[:, : sh.S].float()
+    kr = inp.k[:, : sh.S].float()
+    vr = inp.v_t[:, :, : sh.S].transpose(1, 2).float()
+    s = torch.bmm(qr, kr.transpose(1, 2)) / math.sqrt(d)
+    ref_lse = torch.logsumexp(s, -1)
+    ref = torch.bmm(torch.softmax(s, -1), vr)
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2, f"O max abs err {err}"
+    lerr = (lse - ref_lse).abs().max().item()
+    assert lerr <= 2e-3, f"LSE max abs err {lerr}"
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("nv,text,text_first", [(2048, 0, False), (700, 50, True), (504, 40, False)])
+def test_fmha_block_sparse_vs_oracle(d, nv, text, text_first):
+    lay = _layout(nv, text, text_first)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=4)
+    _, inp = _run_gather(lay, q, k, v, q_mean=False)
+    sh = inp.shapes
+    g = torch.Generator().manual_seed(5)
+    part = torch.rand(sh.banks, sh.nB, sh.nB, generator=g) < 0.3
+    if nv % 128:
+        part[:, -1, :] = True
+        part[:, :, -1] = True
+    out, lse = _fmha(inp.q, inp.k, inp.v_t, part.to(DEV), sh.banks, sh.S, d, nv, False)
+    kmask = orc.kernel_block_mask(part, sh.S, nv)
+    ro, rl = orc.masked_attention(inp.q[:, : sh.S].float().cpu(), inp.k[:, : sh.S].float().cpu(),
+                                  inp.v_t[:, :, : sh.S].transpose(1, 2).float().cpu(), kmask, 1 / math.sqrt(d))
+    err = (out.float().cpu() - ro).abs().max().item()
+    assert err <= 2e-2, f"O max abs err {err}"
+    lerr = (lse.cpu() - rl).abs().max().item()
+    assert lerr <= 2e-3, f"LSE max abs err {lerr}"
+
+
+def test_fmha_native_output_positions():
+    nv, text, d = 700, 50, 64
+    lay = _layout(nv, text, True)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=6)
+    _, inp = _run_gather(lay, q, k, v, q_mean=False)
+    sh = inp.shapes
+    out_r, lse_r = _fmha(inp.q, inp.k, inp.v_t, None, sh.banks, sh.S, d, nv, True)
+    out_n, lse_n = _fmha(inp.q, inp.k, inp.v_t, None, sh.banks, sh.S, d, nv, True,
+                         out_pos=lay.gather_rows(torch.device(DEV)))
+    fwd = lay.gather_rows(torch.device(DEV)).long()
+    assert torch.equal(out_n[:, fwd], out_r)
+    assert torch.equal(lse_n[:, fwd], lse_r)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("nv,text,text_first", [(2048, 0, False), (700, 50, True)])
+def test_closure_statistics_vs_oracle(d, nv, text, text_first):
+    from recap_b200 import _lib as lib
+
+    lay = _layout(nv, text, text_first)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=7)
+    sa, inp = _run_gather(lay, q, k, v, q_mean=False)
+    sh = inp.shapes
+    ctx = sa.coarse_tail_context(inp, 1 / math.sqrt(d))
+    torch.cuda.synchronize()
+    k_r = inp.k[:, : sh.S].float().cpu()
+    v_r = inp.v_t[:, :, : sh.S].transpose(1, 2).float().cpu()
+    km, counts = orc.pool_blocks(k_r, nv)
+    cvk = orc.cross_covariance(k_r, v_r, km, counts, nv)
+    assert torch.allclose(ctx["cvk"].cpu(), cvk, atol=1e-4, rtol=1e-3), (ctx["cvk"].cpu() - cvk).abs().max()
+    basis = ctx["basis"].cpu()
+    var = orc.fold_rank(orc.rotated_variance(k_r, basis, nv), 4)
+    assert torch.allclose(ctx["variance"].cpu(), var, atol=1e-4, rtol=1e-3), (ctx["variance"].cpu() - var).abs().max()
+    # the basis is an ordered eigenbasis of the pooled within-block scatter
+    scat = orc.within_block_scatter(k_r, km, counts, nv)
+    evals = torch.linalg.eigvalsh(scat.double())
+    proj = torch.einsum("bdi,bde,bei->bi", basis.double(), scat.double(), basis.double())
+    assert torch.allclose(torch.sort(proj, -1).values, evals, atol=1e-3, rtol=1e-3)
+    eye = torch.eye(d, dtype=torch.float64).expand(sh.banks, d, d)
+    assert torch.allclose(basis.double().transpose(1, 2) @ basis.double(), eye, atol=1e-4)
+    pooled = (orc.rotated_variance(k_r, basis, nv) * counts.view(1, -1, 1)).sum(1)
+    assert bool((pooled[:, :-1] >= pooled[:, 1:] - 1e-4 * pooled.abs().max()).all()), "basis not ordered"
+    assert torch.equal(ctx["basis_t"].float().cpu(), basis.transpose(1, 2).to(torch.bfloat16).float())
+    del lib
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("nv,text,text_first", [(2048, 0, False), (700, 50, True)])
+def test_coarse_tail_vs_oracle(d, nv, text, text_first):
+    lay = _layout(nv, text, text_first)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=8)
+    sa, inp = _run_gather(lay, q, k, v, q_mean=True)
+    sh = inp.shapes
+    scale = 1 / math.sqrt(d)
+    part = sa.head_partition(inp, scale)
+    ctx = sa.coarse_tail_context(inp, scale)
+    old = torch.randn(sh.banks, sh.rows, generator=torch.Generator().manual_seed(9)).to(DEV)
+    out, lse, center = sa.coarse_tail_apply(inp, ctx, part.reshape(sh.banks, sh.nB, sh.nB), scale, old_lse=old)
+    torch.cuda.synchronize()
+    q_r = inp.q[:, : sh.S].float().cpu()
+    k_r = inp.k[:, : sh.S].float().cpu()
+    v_r = inp.v_t[:, :, : sh.S].transpose(1, 2).float().cpu()
+    km, counts = orc.pool_blocks(k_r, nv)
+    vm, _ = orc.pool_blocks(v_r, nv)
+    basis = ctx["basis"].cpu()
+    var = ctx["variance"].cpu()
+    qsq = orc.rotated_query_square(q_r[:, :nv], basis, torch.bfloat16)
+    drift = orc.value_drift(q_r[:, :nv], ctx["cvk"].cpu(), scale, torch.bfloat16)
+    ro, rl = orc.coarse_tail(q_r, km, vm, var, counts, part.reshape(sh.banks, sh.nB, sh.nB).cpu(), qsq, drift,
+                             scale, 2.0, sh.rows, torch.bfloat16)
+    err = (out.float().cpu() - ro).abs().max().item()
+    assert err <= 2e-2, f"coarse O max abs err {err}"
+    fin = torch.isfinite(rl)
+    assert torch.equal(torch.isfinite(lse.cpu()), fin)
+    lerr = (lse.cpu()[fin] - rl[fin]).abs().max().item()
+    assert lerr <= 2e-3, f"coarse LSE err {lerr}"
+    rc = orc.drift_center(rl, old.cpu())
+    assert torch.allclose(center.cpu(), rc, atol=1e-3)
+
+
+def test_refresh_detail_vs_oracle():
+    from recap_b200 import _lib as lib
+
+    banks, nv, text, d = 2, 700, 50, 64
+    S = nv + text
+    rows = (nv // 128) * 128
+    g = torch.Generator().manual_seed(10)
+    perm = torch.randperm(nv, generator=g)
+    full_o = torch.randn(banks, S, d, generator=g).to(torch.bfloat16)
+    full_lse = torch.randn(banks, S, generator=g) + 4
+    head_o = torch.randn(banks, S, d, generator=g).to(torch.bfloat16)
+    head_lse = full_lse[:, (text + perm).tolist() + list(range(text))] - torch.rand(banks, S, generator=g) * 2
+    go = torch.randn(banks, rows, d, generator=g).to(torch.bfloat16)
+    gl = torch.randn(banks, rows, generator=g) + 2
+    det0 = (torch.randn(banks, rows, d, generator=g) * 0.1).half()
+    dl0 = torch.randn(banks, rows, generator=g) * 0.1
+    old = gl + torch.randn(banks, rows, generator=g) * 0.1
+    center = (gl - old).mean(1)
+    det = det0.clone().to(DEV)
+    dl = dl0.clone().to(DEV)
+    n = lib.load().recap_refresh_partials(banks, nv)
+    partials = torch.empty(n, 2, device=DEV)
+    stats = torch.zeros(2, device=DEV)
+    dv = lambda t: t.contiguous().to(DEV)  # noqa: E731
+    lib.call("recap_refresh_detail", lib.ptr(dv(full_o)), lib.ptr(dv(full_lse)), lib.ptr(dv(head_o)),
+             lib.ptr(dv(head_lse)), lib.ptr(dv(go)), lib.ptr(dv(gl)), lib.ptr(perm.to(torch.int32).to(DEV)), banks, S,
+             d, nv, text, lib.ptr(det), lib.ptr(dl), 1, lib.ptr(dv(old)), lib.ptr(dv(center)), lib.ptr(partials),
+             lib.ptr(stats), lib.stream_handle(torch.device(DEV)))
+    torch.cuda.synchronize()
+    rdet, rdl, rstats = orc.refresh_detail(full_o.float(), full_lse, head_o.float(), head_lse, go.float(), gl,
+                                           perm.numpy(), text, det0.float(), dl0, old, center)
+    assert (det.float().cpu() - rdet.float()).abs().max() <= 2e-3 * max(1.0, float(rdet.float().abs().max()))
+    assert torch.allclose(dl.cpu(), rdl, atol=1e-4)
+    assert torch.allclose(stats.cpu(), rstats.float(), rtol=1e-4)
