@@ -1,0 +1,368 @@
+"""Benchmark: RECAP's corrected sparse attention operator on B200.
+
+Workload: one HunyuanVideo-shaped 720p 129-frame attention layer,
+24 heads x 128, 118800 video tokens (33x45x80 Hilbert-ordered) + 256 text tokens
+(text last), keep ratio 0.1 (93 of 929 key blocks), refinement bank of all heads in HBM.
+A step is one corrected SPARSE layer call through ``recap_b200.Operator.attend`` (the
+reference-facing API); one REFRESH precedes the steps.  With N GPUs the 24 heads are
+split N ways (one process per GPU, no collective inside a SPARSE step): the layer call's
+time is the max over ranks, so the scaling is strong.
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU path (the
+oracle restatement, see oracle/cpu_baseline.py) instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+WORKLOAD = dict(name="hunyuan720p_layer", grid=(33, 45, 80), heads=24, dim=128, text=256, text_first=False,
+                density=0.1)
+METRIC = "corrected sparse-attn us/layer call (HunyuanVideo-720p layer, SPARSE step)"
+UNIT = "us/layer"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile-steps", type=int, default=3, help="extra steps with per-kernel CUDA events")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------- data
+
+
+def synth_qkv(grid, heads: range, dim: int, text: int, text_first: bool, seed: int, device, rank: int = 16,
+              noise: float = 0.5):
+    """Seeded Q/K/V [1, len(heads), S, dim] bf16 with per-frame spatially smooth low-rank
+    structure (sum of 4 low-frequency cosines per factor, per-frame phase drift) plus
+    noise; text tokens N(0,1).  Generated per head on the device."""
+    T, H, W = grid
+    nv = T * H * W
+    tt = torch.arange(T, dtype=torch.float32, device=device).view(T, 1, 1)
+    yy = (torch.arange(H, dtype=torch.float32, device=device) / H).view(1, H, 1)
+    xx = (torch.arange(W, dtype=torch.float32, device=device) / W).view(1, 1, W)
+    out = []
+    for tensor in range(3):
+        x = torch.empty(1, len(heads), nv + text, dim, dtype=torch.bfloat16, device=device)
+        for i, h in enumerate(heads):
+            g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + tensor * 10_007 + h)
+            u = torch.randn(rank, dim, generator=g, device=device) / math.sqrt(rank)
+            amp = torch.randn(rank, 4, generator=g, device=device)
+            ky = torch.randint(-2, 3, (rank, 4), generator=g, device=device).float()
+            kx = torch.randint(-2, 3, (rank, 4), generator=g, device=device).float()
+            ph = torch.rand(rank, 4, generator=g, device=device) * 2 * math.pi
+            dr = (torch.rand(rank, 4, generator=g, device=device) - 0.5) * 0.6
+            f = torch.zeros(rank, T, H, W, device=device)
+            for c in range(4):
+                v = lambda a: a[:, c].view(rank, 1, 1, 1)  # noqa: E731
+                f += v(amp) * torch.cos(2 * math.pi * (v(ky) * yy + v(kx) * xx) + v(ph) + v(dr) * tt)
+            vid = f.reshape(rank, nv).T @ u + noise * torch.randn(nv, dim, generator=g, device=device)
+            txt = torch.randn(text, dim, generator=g, device=device)
+            x[0, i] = torch.cat([txt, vid]) if text_first else torch.cat([vid, txt])
+        out.append(x)
+    return out
+
+
+def perturbed(xs, seed: int, device, eps: float = 0.05):
+    g = torch.Generator(device=device).manual_seed(seed)
+    return [(x.float() + eps * torch.randn(x.shape, generator=g, device=device)).to(x.dtype) for x in xs]
+
+
+# ----------------------------------------------------------------------------- helpers
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"recap_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        try:
+            rows = [r.split(",") for r in self.path.read_text().strip().splitlines()]
+        except Exception:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = sorted(float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit())
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def kept_tile_flops(partition: torch.Tensor, S: int, nv: int, dim: int) -> float:
+    """sum over banks and kept 128x128 tiles of 4 * m_i * n_j * d with the real token counts
+    of the blocks on the reordered sequence."""
+    banks = partition.shape[0] * partition.shape[1]
+    nb = partition.shape[-1]
+    NB = (S + 127) // 128
+    shared = nv % 128 != 0 and S > nv
+    ds = nb - 1 if shared else nb
+    counts = torch.full((NB,), 128.0, dtype=torch.float64)
+    counts[-1] = S - 128 * (NB - 1)
+    part = partition.reshape(banks, nb, nb).to(torch.float64).cpu()
+    mask = torch.zeros(banks, NB, NB, dtype=torch.float64)
+    mask[:, :nb, :nb] = part
+    mask[:, ds:, :] = 1
+    mask[:, :, ds:] = 1
+    per_bank = torch.einsum("bij,i,j->b", mask, counts, counts)
+    return float(per_bank.sum()) * 4 * dim
+
+
+def peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"bf16_tflops": d["bf16_tflops"], "bf16_tflops_sustained": d["bf16_tflops_sustained"],
+                "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def traffic_per_launch() -> float | None:
+    """DRAM bytes of one sparse-step launch at the bench workload, from the committed ncu
+    summary (profiles/sparse_step_hunyuan720p.json), or None."""
+    path = REPO / "profiles" / "sparse_step_hunyuan720p.json"
+    if not path.exists():
+        return None
+    try:
+        return float(json.loads(path.read_text())["dram_bytes_per_launch_full_workload"])
+    except Exception:
+        return None
+
+
+# ----------------------------------------------------------------------------- our arm
+
+
+def run_ours(args) -> None:
+    import torch.distributed as dist
+
+    from recap_b200 import REFRESH, SPARSE, Operator, OperatorConfig
+    from recap_b200.sparse import Layout, SparseGeometry, hilbert_permutation
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        group = dist.group.WORLD
+    w = WORKLOAD
+    H = w["heads"]
+    if H % world:
+        raise SystemExit(f"{H} heads do not split over {world} GPUs")
+    hs = range(rank * H // world, (rank + 1) * H // world)
+    perm = hilbert_permutation(w["grid"])
+    layout = Layout.from_permutation(perm, text_tokens=w["text"], text_first=w["text_first"])
+    geo = SparseGeometry.build(layout, 128)
+    cfg = OperatorConfig(head_density=w["density"])
+    op = Operator.build(cfg, geo, n_layers=1, process_group=group)
+    nv = layout.video_tokens
+    S = nv + w["text"]
+    d = w["dim"]
+
+    x0 = synth_qkv(w["grid"], hs, d, w["text"], w["text_first"], seed=0, device=dev)
+    op.begin_step(0, REFRESH)
+    op.attend(0, *x0)
+    torch.cuda.synchronize()
+    x1 = perturbed(x0, 1, dev)
+    x2 = perturbed(x1, 2, dev)
+    del x0
+    inputs = [x1, x2]
+
+    # refresh timing (revalidating refresh on x2, then restore the bank state with x1's)
+    op.begin_step(1, REFRESH)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    op.attend(0, *x2)
+    t1.record()
+    torch.cuda.synchronize()
+    refresh_ms = t0.elapsed_time(t1)
+    op.drain_validation()
+
+    op.begin_step(2, SPARSE)
+    for i in range(args.warmup):
+        op.attend(0, *inputs[i % 2])
+    torch.cuda.synchronize()
+    if group is not None:
+        dist.barrier(group=group)
+    launches_before = op.launches.count
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clk:
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(args.steps):
+            out = op.attend(0, *inputs[i % 2])
+        end.record()
+        torch.cuda.synchronize()
+    if group is not None:
+        dist.barrier(group=group)
+    gpu_launches = op.launches.count - launches_before
+    elapsed = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=dev)
+    if group is not None:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX, group=group)
+    ms_per_step = float(elapsed.item()) / args.steps
+    del out
+
+    # per-kernel times over a few more steps (events on the launching stream)
+    op.launches.timing = True
+    for i in range(args.profile_steps):
+        op.attend(0, *inputs[i % 2])
+    times = op.launches.take_times()
+    op.launches.timing = False
+    kernels_ms = {k: sum(v) / len(v) for k, v in times.items()}
+    fmha_ms = kernels_ms.get("recap_sparse_step")
+    flops = kept_tile_flops(op.banks[0][0].partition, S, nv, d)
+    flops_t = torch.tensor([flops], dtype=torch.float64, device=dev)
+    if group is not None:
+        dist.all_reduce(flops_t, group=group)
+    pk = peaks()
+    achieved = flops / (fmha_ms * 1e-3) / 1e12 if fmha_ms else None
+    traffic = traffic_per_launch()
+
+    # end to end through the API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        host = [[t.cpu().pin_memory() for t in xs] for xs in inputs]
+        dev_in = [torch.empty_like(t) for t in inputs[0]]
+        out_host = torch.empty(1, len(hs), S, d, dtype=torch.bfloat16).pin_memory()
+        for i in range(2):
+            for dst, src in zip(dev_in, host[i % 2]):
+                dst.copy_(src, non_blocking=True)
+            out_host.copy_(op.attend(0, *dev_in), non_blocking=True)
+        torch.cuda.synchronize()
+        if group is not None:
+            dist.barrier(group=group)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            for dst, src in zip(dev_in, host[i % 2]):
+                dst.copy_(src, non_blocking=True)
+            out_host.copy_(op.attend(0, *dev_in), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if group is not None:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX, group=group)
+        h2d = sum(t.numel() * t.element_size() for t in host[0])
+        e2e = {"value": round(float(et.item()) / args.steps * 1000.0, 1), "unit": UNIT,
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": out_host.numel() * 2 * world}
+        del host, dev_in, out_host
+    op.check_device_status()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.cpu_baseline import time_sparse_sample
+
+        cpu = time_sparse_sample(op, inputs[0], layout, w)
+
+    if rank == 0:
+        dense_flops = 4.0 * S * S * d * H
+        line = {
+            "metric": METRIC, "value": round(ms_per_step * 1000.0, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded smooth low-rank (rank 16) + 0.5 noise Q/K/V, 0.05 perturbation per step",
+            "config": {"workload": w["name"], "heads": H, "head_dim": d, "video_tokens": nv, "text_tokens": w["text"],
+                       "seq_len": S, "key_blocks": geo.n_blocks, "keep": max(1, round(w["density"] * geo.n_blocks)),
+                       "parallelism": f"heads/{world}", "bank": "HBM",
+                       "l2": "inputs 2.19 GB per step > 126 MB L2 (no flush needed)"},
+            "dense_equiv_tflops": round(dense_flops / (ms_per_step * 1e-3) / 1e12, 1),
+            "refresh_us": round(refresh_ms * 1000.0, 1),
+            "kernels_ms": {k: round(v, 4) for k, v in kernels_ms.items()},
+            "roofline": {
+                "kernel": "recap_sparse_step (block-sparse FMHA + corrected merge)",
+                "bound": "tensor", "achieved": round(achieved, 1) if achieved else None,
+                "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16_tflops_sustained"], 4) if achieved else None,
+                "peak_kind": f"bf16 sustained ({pk['source']})",
+                "algorithmic_flops_per_launch": flops,
+                "traffic": traffic,
+            },
+            "gpu_launches": gpu_launches,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if group is not None:
+        dist.barrier(group=group)
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from oracle.cpu_baseline import reference_arm
+
+    line = reference_arm(WORKLOAD, METRIC, UNIT, steps=args.steps, warmup=args.warmup)
+    line.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup})
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)

@@ -27,10 +27,9 @@ enum : int {
   kStatusBadList = 105,
 };
 
-// Upper bound on try_wait polls of one mbarrier wait (each poll may itself
-// suspend for a hardware-defined time).  About a second or more of waiting on a
-// B200 before the kernel gives up.
-constexpr uint32_t kMaxPolls = 1u << 24;
+// Longest a single mbarrier wait may last before the kernel gives up (ns of
+// %globaltimer).  Every legitimate wait of these kernels lasts microseconds.
+constexpr uint64_t kWaitNs = 3000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -73,18 +72,48 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Wait for the phase with the given parity to complete.  Returns false when the
-// wait ran out or another role of the CTA aborted; in both cases the CTA-local
-// abort flag is set and (on timeout) the status word records `code`.
+// wait ran out of time or another role of the CTA aborted; in both cases the
+// CTA-local abort flag is set and (on timeout) the status word records `code`.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, int code) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+  uint64_t start = 0;
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 255u && *abort_flag) return false;
+    if ((i & 63u) == 63u) {
+      if (*abort_flag) return false;
+      const uint64_t now = global_ns();
+      if (start == 0) {
+        start = now;
+      } else if (now - start > kWaitNs) {
+        *abort_flag = 1;
+        if (status) atomicCAS(status, 0, code);
+        return false;
+      }
+    }
   }
-  *abort_flag = 1;
-  if (status) atomicCAS(status, 0, code);
-  return false;
+}
+
+// Bounded wait used on the way out (draining copies or MMAs in flight): gives up
+// silently after kWaitNs.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  uint64_t start = 0;
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((i & 63u) == 63u) {
+      const uint64_t now = global_ns();
+      if (start == 0)
+        start = now;
+      else if (now - start > kWaitNs)
+        return;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- TMA

@@ -177,11 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int first = i > NST ? i - NST : 0;
       for (int k = first; k < i; ++k) {
         const int slot = k % NST;
-        for (uint32_t p = 0; p < kMaxPolls && !mbar_try_wait(bars.full + slot, (k / NST) & 1); ++p) {
-        }
+        mbar_drain(bars.full + slot, (k / NST) & 1);
       }
-      for (uint32_t p = 0; p < kMaxPolls && !mbar_try_wait(bars.qfull, 0); ++p) {
-      }
+      mbar_drain(bars.qfull, 0);
     }
   } else if (warp == 1) {
     // ================================================================ MMA issuer
@@ -242,8 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) ok = issue_pv(n_kv - 1);
       // All MMAs issued by this thread complete before TMEM is released.
       mma_commit(bars.done);
-      for (uint32_t p = 0; p < kMaxPolls && !mbar_try_wait(bars.done, 0); ++p) {
-      }
+      mbar_drain(bars.done, 0);
     }
   } else if (warp >= kSoftmaxWarp0) {
     // ================================================================ softmax + epilogue
@@ -341,11 +338,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok) {
       tc_fence_after();
       const int r = qblock * 128 + t;  // reordered row
-      const bool in_seq = r < args.S;
+      int pos = r < args.S ? (args.out_pos ? args.out_pos[r] : r) : -1;
+      const bool in_seq = pos >= 0 && pos < args.S;  // a corrupt index writes nothing
       const float inv_l = 1.f / l_run;
       const float lse_h = (m_run + __log2f(l_run)) * 0.69314718055994531f;
       const size_t bank_rows = static_cast<size_t>(bank) * args.S;
-      const int pos = in_seq ? (args.out_pos ? args.out_pos[r] : r) : 0;
+      if (!in_seq) pos = 0;
       if (args.epilogue == 0) {
         __nv_bfloat16* orow = args.o + (bank_rows + pos) * D;
 #pragma unroll 1

@@ -59,7 +59,8 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
       uint4 val = make_uint4(0, 0, 0, 0);
       if (r < a.S) {
         const int64_t native = a.src_row[r];
-        val = *reinterpret_cast<const uint4*>(base + native * a.stride_s[t] + ch * 8);
+        if (native >= 0 && native < a.S)  // a corrupt index reads nothing out of bounds
+          val = *reinterpret_cast<const uint4*>(base + native * a.stride_s[t] + ch * 8);
       }
       if (t == 0 && a.qr) {
         *reinterpret_cast<uint4*>(a.qr + (static_cast<size_t>(bank) * a.S_pad + r) * D + ch * 8) = val;

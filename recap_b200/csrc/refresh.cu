@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(256) refresh_kernel(const RefreshArgs a) {
     const int r = blockIdx.x * kRowsPerCta + p * RPP + rsub;
     if (r >= a.rows) continue;
     const int n = a.video_offset + a.perm[r];
+    if (n < 0 || n >= a.S) continue;  // a corrupt permutation reads nothing out of bounds
     const size_t srow = static_cast<size_t>(bank) * a.S;
     const size_t vrow = static_cast<size_t>(bank) * a.rows + r;
     const float lf = a.full_lse[srow + n];

@@ -119,7 +119,8 @@ def test_pool_select_ties_take_lower_index():
     km = torch.zeros(banks, nB, d)
     km[0, :, 0] = torch.tensor([0.5, 2.0, 1.0, 1.0, 1.0, 1.0, 0.0, 3.0])
     part = torch.empty(banks, nB, nB, dtype=torch.bool, device=DEV)
-    lib.call("recap_pool_select", lib.ptr(qm.to(DEV)), lib.ptr(km.to(DEV)), banks, nB, d, keep, 1.0, nB * 128, 128,
+    qm_d, km_d = qm.to(DEV), km.to(DEV)
+    lib.call("recap_pool_select", lib.ptr(qm_d), lib.ptr(km_d), banks, nB, d, keep, 1.0, nB * 128, 128,
              lib.ptr(part), lib.stream_handle(torch.device(DEV)))
     # scores per row: [0.5, 2, 1, 1, 1, 1, 0, 3] -> top 3 = {7, 1, 2} (block 2 wins the tie)
     assert part[0, 0].cpu().tolist() == [False, True, True, False, False, False, False, True]
@@ -284,10 +285,14 @@ def test_refresh_detail_vs_oracle():
     n = lib.load().recap_refresh_partials(banks, nv)
     partials = torch.empty(n, 2, device=DEV)
     stats = torch.zeros(2, device=DEV)
-    dv = lambda t: t.contiguous().to(DEV)  # noqa: E731
-    lib.call("recap_refresh_detail", lib.ptr(dv(full_o)), lib.ptr(dv(full_lse)), lib.ptr(dv(head_o)),
-             lib.ptr(dv(head_lse)), lib.ptr(dv(go)), lib.ptr(dv(gl)), lib.ptr(perm.to(torch.int32).to(DEV)), banks, S,
-             d, nv, text, lib.ptr(det), lib.ptr(dl), 1, lib.ptr(dv(old)), lib.ptr(dv(center)), lib.ptr(partials),
+    # keep every device buffer referenced until the kernel has run (a temporary freed
+    # while its pointer is in flight would be reused by the caching allocator)
+    dev = {name: t.contiguous().to(DEV) for name, t in dict(
+        full_o=full_o, full_lse=full_lse, head_o=head_o, head_lse=head_lse, go=go, gl=gl, old=old, center=center,
+        perm=perm.to(torch.int32)).items()}
+    lib.call("recap_refresh_detail", lib.ptr(dev["full_o"]), lib.ptr(dev["full_lse"]), lib.ptr(dev["head_o"]),
+             lib.ptr(dev["head_lse"]), lib.ptr(dev["go"]), lib.ptr(dev["gl"]), lib.ptr(dev["perm"]), banks, S,
+             d, nv, text, lib.ptr(det), lib.ptr(dl), 1, lib.ptr(dev["old"]), lib.ptr(dev["center"]), lib.ptr(partials),
              lib.ptr(stats), lib.stream_handle(torch.device(DEV)))
     torch.cuda.synchronize()
     rdet, rdl, rstats = orc.refresh_detail(full_o.float(), full_lse, head_o.float(), head_lse, go.float(), gl,
