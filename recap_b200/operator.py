@@ -34,11 +34,39 @@ import torch
 from . import _lib
 from .config import OperatorConfig
 from .sparse.attention import Launches, LayerInputs, SparseAttention, SparseGeometry
-from .sparse.layout import Layout
+from .sparse.layout import Layout, gather_rows, video_offset, video_permutation_i32
 
 EXACT = "exact"
 REFRESH = "refresh"
 SPARSE = "sparse"
+
+
+def layer_counts_reduce(counts: torch.Tensor, group=None) -> tuple[int, int]:
+    """Sum the (kept, total) overlap counts of this rank's heads over the process group:
+    the reference takes the re-selection decision over the whole layer
+    (recap/operator.py:282-291, 425-428), and with head sharding the layer spans ranks."""
+    if group is not None:
+        import torch.distributed as dist
+
+        dist.all_reduce(counts, group=group)
+    kept, total = (int(x) for x in counts.cpu())
+    return kept, total
+
+
+def keep_partition(kept: int, total: int, min_overlap: float) -> bool:
+    """Keep the old partition iff the new selection overlaps it by at least min_overlap
+    (recap/operator.py:425-428)."""
+    return kept / max(total, 1) >= float(min_overlap)
+
+
+def validation_reduce(total: torch.Tensor, group=None) -> tuple[float, float]:
+    """Sum (sum err^2, sum ref^2) over the process group (recap/operator.py:544-545)."""
+    if group is not None:
+        import torch.distributed as dist
+
+        dist.all_reduce(total, group=group)
+    numerator, denominator = (float(x) for x in total)
+    return numerator, denominator
 
 
 @dataclass
@@ -233,7 +261,7 @@ class Operator:
         self.launches.run(
             "recap_block_sparse_fmha", 1,
             _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), None, sh.banks, sh.S, sh.D,
-            sh.n_video, 1, float(scale), _lib.ptr(self.layout.gather_rows(dev)) if native else None,
+            sh.n_video, 1, float(scale), _lib.ptr(gather_rows(self.layout, dev)) if native else None,
             _lib.ptr(out), _lib.ptr(lse), _lib.ptr(status), _lib.stream_handle(dev),
         )
         return out, lse
@@ -267,12 +295,7 @@ class Operator:
             "recap_partition_overlap", 1, _lib.ptr(new), _lib.ptr(old), new.numel(), _lib.ptr(counts),
             _lib.stream_handle(new.device),
         )
-        if self.process_group is not None:
-            import torch.distributed as dist
-
-            dist.all_reduce(counts, group=self.process_group)
-        kept, total = (int(x) for x in counts.cpu())
-        return kept, total
+        return layer_counts_reduce(counts, self.process_group)
 
     @torch.no_grad()
     def _refresh(self, layer: SparseAttention, bank: DetailBank, query, key, value) -> torch.Tensor:
@@ -309,7 +332,7 @@ class Operator:
             partition = layer.head_partition(inputs, scale)
             if bank.partition is not None:
                 kept, total = self._layer_overlap(partition, bank.partition)
-                if kept / max(total, 1) >= self.config.rerank_min_overlap:
+                if keep_partition(kept, total, self.config.rerank_min_overlap):
                     bank.coarse_lse = coarse_lse.clone()
                     bank.refreshed_at = self.step
                     bank.valid = True
@@ -338,8 +361,8 @@ class Operator:
         self.launches.run(
             "recap_refresh_detail", 1 + (stats is not None),
             _lib.ptr(full_out), _lib.ptr(full_lse), _lib.ptr(head_o), _lib.ptr(head_lse), _lib.ptr(coarse),
-            _lib.ptr(coarse_lse), _lib.ptr(self.layout.video_permutation(dev, torch.int32)), sh.banks, sh.S,
-            sh.D, sh.n_video, self.layout.video_offset, _lib.ptr(bank.value), _lib.ptr(bank.log_mass),
+            _lib.ptr(coarse_lse), _lib.ptr(video_permutation_i32(self.layout, dev)), sh.banks, sh.S,
+            sh.D, sh.n_video, video_offset(self.layout), _lib.ptr(bank.value), _lib.ptr(bank.log_mass),
             1 if stats is not None else 0, _lib.ptr(old_lse), _lib.ptr(center), _lib.ptr(partials),
             _lib.ptr(stats), _lib.stream_handle(dev),
         )
@@ -369,7 +392,7 @@ class Operator:
             _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(bank.partition), sh.banks,
             sh.S, sh.D, sh.n_video, float(scale), _lib.ptr(coarse), _lib.ptr(coarse_lse), _lib.ptr(bank.value),
             _lib.ptr(bank.log_mass), _lib.ptr(bank.coarse_lse), _lib.ptr(center),
-            _lib.ptr(self.layout.gather_rows(dev)), _lib.ptr(out), _lib.ptr(status), _lib.stream_handle(dev),
+            _lib.ptr(gather_rows(self.layout, dev)), _lib.ptr(out), _lib.ptr(status), _lib.stream_handle(dev),
         )
         return out
 
@@ -391,11 +414,7 @@ class Operator:
         if not stats:
             return None
         total = torch.stack(stats).sum(dim=0)
-        if self.process_group is not None:
-            import torch.distributed as dist
-
-            dist.all_reduce(total, group=self.process_group)
-        numerator, denominator = (float(x) for x in total)
+        numerator, denominator = validation_reduce(total, self.process_group)
         error = math.sqrt(numerator / denominator) if denominator > 0.0 else float("inf")
         return min(ages), error
 

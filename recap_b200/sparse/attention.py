@@ -23,7 +23,7 @@ import torch
 
 from .. import _lib
 from ..config import keep_blocks
-from .layout import Layout
+from .layout import Layout, gather_rows, sequence_tokens
 
 BLOCK = 128
 
@@ -52,11 +52,16 @@ class SparseGeometry:
             self.block_counts = self.block_counts.to(device)
 
     def counts_log(self, device: torch.device) -> torch.Tensor:
-        cache = self.__dict__.setdefault("_counts_log", {})
-        key = str(device)
-        if key not in cache:
-            cache[key] = torch.log(self.block_counts.detach().float().cpu()).to(device)
-        return cache[key]
+        return counts_log(self, device)
+
+
+def counts_log(geometry, device: torch.device) -> torch.Tensor:
+    """ln(tokens per video block) on ``device``; works on the reference's SparseGeometry too."""
+    cache = geometry.__dict__.setdefault("_recap_b200_counts_log", {})
+    key = str(device)
+    if key not in cache:
+        cache[key] = torch.log(torch.as_tensor(geometry.block_counts).detach().float().cpu()).to(device)
+    return cache[key]
 
 
 @dataclass
@@ -168,9 +173,9 @@ class SparseAttention:
         means: bool = True,
     ) -> LayerInputs:
         layout = self.geometry.layout
-        if query.shape[-2] != layout.sequence_tokens:
+        if query.shape[-2] != sequence_tokens(layout):
             raise ValueError(
-                f"sequence {query.shape[-2]} != video+text {layout.sequence_tokens}"
+                f"sequence {query.shape[-2]} != video+text {sequence_tokens(layout)}"
             )
         sh = Shapes.of(query, layout.video_tokens)
         dev = query.device
@@ -190,7 +195,7 @@ class SparseAttention:
         self.launches.run(
             "recap_layout_gather", 1,
             _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), strides,
-            sh.batch, sh.heads, sh.S, sh.D, sh.n_video, _lib.ptr(layout.gather_rows(dev)),
+            sh.batch, sh.heads, sh.S, sh.D, sh.n_video, _lib.ptr(gather_rows(layout, dev)),
             _lib.ptr(q_r), _lib.ptr(k_r), _lib.ptr(v_t), _lib.ptr(qm), _lib.ptr(km), _lib.ptr(vm),
             _lib.ptr(kmb), _lib.ptr(vmtb), _lib.stream_handle(dev),
         )
@@ -304,7 +309,7 @@ class SparseAttention:
             "recap_coarse_tail", 1 + (old_lse is not None),
             _lib.ptr(inputs.q), _lib.ptr(context["basis_t"]), _lib.ptr(context["cvk_bf16"]),
             _lib.ptr(inputs.k_mean_bf16), _lib.ptr(context["variance_bf16"]), _lib.ptr(inputs.v_mean_t_bf16),
-            _lib.ptr(partition), _lib.ptr(self.geometry.counts_log(dev)), _lib.ptr(old_lse),
+            _lib.ptr(partition), _lib.ptr(counts_log(self.geometry, dev)), _lib.ptr(old_lse),
             sh.banks, sh.S, sh.D, sh.n_video, float(scale), float(self.config.closure_gate_theta),
             _lib.ptr(out), _lib.ptr(lse), _lib.ptr(partial), _lib.ptr(center), _lib.ptr(status),
             _lib.stream_handle(dev),
