@@ -35,6 +35,7 @@ extern "C" {
 #define RECAP_ERR_LAUNCH 2
 #define RECAP_ERR_DEVICE 3
 #define RECAP_ERR_UNSUPPORTED 4
+#define RECAP_ERR_SCRATCH_LIMIT 5 /* beyond the fixed scratch of recap_refresh_detail_noalloc */
 
 /* values of the device status word */
 #define RECAP_STATUS_TIMEOUT_TMA 101
@@ -157,6 +158,22 @@ int recap_refresh_detail(const void* full_o, const float* full_lse, const void* 
                          int D, int n_video, int video_offset, void* detail_value, float* detail_log_mass,
                          int validate, const float* old_lse, const float* center, float* partials,
                          float* stats, void* stream);
+
+/* recap_refresh_detail without the `partials` scratch argument, for callers that may not
+ * allocate device memory (hosts that pass a plugin only buffers they planned themselves,
+ * or step loops that cannot afford the device synchronisation of cudaMalloc).  It has no
+ * counterpart in the reference.  The validation partial sums live in a 1 MiB array inside
+ * the library, held by every GPU that loads it until the process exits; the call rejects
+ * problems with banks * ceil(rows / 32) > 131072 with RECAP_ERR_SCRATCH_LIMIT.  The first call on a
+ * device looks the array's device address up (cudaGetSymbolAddress), so make that first
+ * call before any stream capture.  All calls share the one array: calls that may overlap
+ * on the GPU (different streams, or different host threads) race and must be ordered by
+ * the caller.  Nothing in the array needs clearing: each call writes every entry it reads. */
+int recap_refresh_detail_noalloc(const void* full_o, const float* full_lse, const void* head_o,
+                                 const float* head_lse, const void* coarse_out, const float* coarse_lse,
+                                 const int32_t* perm, int banks, int S, int D, int n_video, int video_offset,
+                                 void* detail_value, float* detail_log_mass, int validate, const float* old_lse,
+                                 const float* center, float* stats, void* stream);
 
 #ifdef __cplusplus
 }

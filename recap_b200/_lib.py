@@ -21,6 +21,7 @@ RECAP_ERR_SHAPE = 1
 RECAP_ERR_LAUNCH = 2
 RECAP_ERR_DEVICE = 3
 RECAP_ERR_UNSUPPORTED = 4
+RECAP_ERR_SCRATCH_LIMIT = 5
 
 STATUS_NAMES = {
     101: "TMA wait timed out",
@@ -49,6 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "recap_sparse_step": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "recap_refresh_partials": (_I, [_I, _I]),
     "recap_refresh_detail": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
+    "recap_refresh_detail_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
 }
 
 _lib = None
@@ -90,6 +92,11 @@ def check(rc: int, what: str) -> None:
         raise ValueError(f"{what}: invalid shape, stride or alignment")
     if rc == RECAP_ERR_UNSUPPORTED:
         raise ValueError(f"{what}: unsupported configuration")
+    if rc == RECAP_ERR_SCRATCH_LIMIT:
+        raise ValueError(
+            f"{what}: the problem needs more validation scratch than the library's fixed array "
+            "holds (banks * ceil(rows / 32) must be <= 131072)"
+        )
     raise RuntimeError(f"{what}: CUDA launch failed (code {rc})")
 
 

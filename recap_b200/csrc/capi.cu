@@ -331,4 +331,37 @@ int recap_refresh_detail(const void* full_o, const float* full_lse, const void* 
   return launch_refresh(a, static_cast<cudaStream_t>(stream));
 }
 
+int recap_refresh_detail_noalloc(const void* full_o, const float* full_lse, const void* head_o,
+                                 const float* head_lse, const void* coarse_out, const float* coarse_lse,
+                                 const int32_t* perm, int banks, int S, int D, int n_video, int video_offset,
+                                 void* detail_value, float* detail_log_mass, int validate, const float* old_lse,
+                                 const float* center, float* stats, void* stream) {
+  Geom g;
+  if (!geom(S, n_video, &g) || !d_ok(D) || banks <= 0) return kErrShape;
+  if (validate && stats == nullptr) return kErrShape;
+  if ((old_lse == nullptr) != (center == nullptr)) return kErrShape;
+  if (old_lse != nullptr && !validate) return kErrShape;
+  RefreshArgs a{};
+  a.banks = banks;
+  a.S = S;
+  a.D = D;
+  a.rows = g.rows;
+  a.video_offset = video_offset;
+  a.full_o = static_cast<const __nv_bfloat16*>(full_o);
+  a.full_lse = full_lse;
+  a.head_o = static_cast<const __nv_bfloat16*>(head_o);
+  a.head_lse = head_lse;
+  a.go = static_cast<const __nv_bfloat16*>(coarse_out);
+  a.gl = coarse_lse;
+  a.perm = perm;
+  a.det = static_cast<__half*>(detail_value);
+  a.dl = detail_log_mass;
+  a.validate = validate;
+  a.ogl = old_lse;
+  a.center = center;
+  a.partials = nullptr;
+  a.stats = stats;
+  return launch_refresh_noalloc(a, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -17,6 +17,7 @@ enum : int {
   kErrLaunch = 2,   // CUDA launch or API failure
   kErrDevice = 3,   // a kernel reported a device-side timeout (see the status word)
   kErrUnsupported = 4,
+  kErrScratchLimit = 5,  // larger than the fixed scratch of a no-allocation entry point
 };
 
 // ------------------------------------------------------------------ layout gather + pooling
@@ -155,6 +156,8 @@ struct RefreshArgs {
 };
 int refresh_partials_count(int banks, int rows);
 int launch_refresh(const RefreshArgs& a, cudaStream_t s);
+// same, with the validation partials in a static device array (no caller scratch)
+int launch_refresh_noalloc(RefreshArgs a, cudaStream_t s);
 
 // ------------------------------------------------------------------ tensor maps
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix, box = 64 columns x box_rows,

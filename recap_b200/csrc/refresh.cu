@@ -10,6 +10,8 @@
 // given) is compared with the dense output first: sum (old - of)^2 and sum of^2.  The reference
 // adds those with fp32 atomics; here every CTA writes its two partial sums and one more kernel
 // adds them in a fixed order, so the result is deterministic.
+#include <mutex>
+
 #include "kernels.h"
 
 namespace recap {
@@ -197,6 +199,53 @@ int launch_refresh(const RefreshArgs& a, cudaStream_t s) {
     if (cudaGetLastError() != cudaSuccess) return kErrLaunch;
   }
   return kOk;
+}
+
+
+// ---------------------------------------------------------------------------------------
+// Variant for callers that may not allocate device memory.
+//
+// Some hosts hand a plugin only the buffers they planned themselves and forbid it any
+// device allocation of its own (serving runtimes with a fixed memory plan, custom-op
+// interfaces that pass in every buffer), and cudaMalloc also synchronises the device,
+// which a step loop cannot afford.  recap_refresh_detail needs one scratch buffer, the
+// per-CTA validation partial sums; this variant keeps them in the file-scope device
+// array below instead of a caller buffer.  Its size is fixed: at most
+// kNoAllocMaxPairs (bank, 32-row) chunks, i.e. banks * ceil(rows / 32) <= 131072, which
+// covers a 24-head HunyuanVideo-720p layer (89088 chunks).  Every GPU that loads the
+// library holds the array (1 MiB) until the process exits.
+constexpr int kNoAllocMaxPairs = 131072;
+static __device__ __align__(256) float g_refresh_scratch[2 * kNoAllocMaxPairs];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+float* g_scratch_ptr[kMaxDevices] = {};
+}  // namespace
+
+// Device address of the scratch array on the current device, looked up once per device
+// (the host-side symbol is not a device address).  Returns nullptr on failure.
+static float* refresh_scratch_for_current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_refresh_scratch) != cudaSuccess) return nullptr;
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  return g_scratch_ptr[dev];
+}
+
+int launch_refresh_noalloc(RefreshArgs a, cudaStream_t s) {
+  if (a.validate) {
+    if (refresh_partials_count(a.banks, a.rows) > kNoAllocMaxPairs) return kErrScratchLimit;
+    float* scratch = refresh_scratch_for_current_device();
+    if (scratch == nullptr) return kErrLaunch;
+    // every CTA writes its own pair before the sum reads it: nothing needs clearing
+    a.partials = scratch;
+  }
+  return launch_refresh(a, s);
 }
 
 }  // namespace recap
