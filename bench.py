@@ -43,6 +43,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile-steps", type=int, default=3, help="extra steps with per-kernel CUDA events")
+    p.add_argument("--heads", type=int, default=None,
+                   help="run only this many of the layer's heads (small cases for ncu captures)")
     return p.parse_args()
 
 
@@ -199,7 +201,10 @@ def run_ours(args) -> None:
 
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
         group = dist.group.WORLD
-    w = WORKLOAD
+    w = dict(WORKLOAD)
+    if args.heads:
+        w["heads"] = int(args.heads)
+        w["name"] = f'{w["name"]}_{args.heads}heads'
     H = w["heads"]
     if H % world:
         raise SystemExit(f"{H} heads do not split over {world} GPUs")
