@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define RECAP_B200_ABI_VERSION 1
+#define RECAP_B200_ABI_VERSION 2
 
 #define RECAP_OK 0
 #define RECAP_ERR_SHAPE 1
@@ -55,11 +55,33 @@ int recap_abi_version(void);
  *   v_transposed   [banks, D, S_pad] bf16 out, reordered V transposed (nullable)
  *   q_mean, k_mean, v_mean    [banks, nB, D] fp32 block means over video tokens (nullable)
  *   k_mean_bf16    [banks, nB_pad, D] bf16 (nullable), v_mean_t_bf16 [banks, D, nB_pad] bf16
- *                  (nullable); their padding rows/columns must be zero. */
+ *                  (nullable); their padding rows/columns must be zero.
+ *   k_centred_t    [banks, D, S_pad] bf16 out (nullable): block-centred video keys k - kbar,
+ *                  transposed, zero outside the video tokens (operand of recap_value_key_covariance)
+ *   basis, rank, variance, variance_bf16 (nullable together): with a basis U [banks, D, D] fp32
+ *                  and 0 < rank < D, rank <= recap_gather_max_rank(), the per-block key
+ *                  variances in U folded to `rank` (rotated_leaf_moments_triton + fold_rank,
+ *                  recap/kernels/closure_stats.py:192-242, recap/sparse/closure.py:96-104):
+ *                  variance [banks, nB, D] fp32, variance_bf16 [banks, nB_pad, D]. */
 int recap_layout_gather(const void* q, const void* k, const void* v, const int64_t* strides, int batch,
                         int heads, int S, int D, int n_video, const int32_t* src_row, void* q_reordered,
                         void* k_reordered, void* v_transposed, float* q_mean, float* k_mean,
-                        float* v_mean, void* k_mean_bf16, void* v_mean_t_bf16, void* stream);
+                        float* v_mean, void* k_mean_bf16, void* v_mean_t_bf16, void* k_centred_t,
+                        const float* basis, int rank, float* variance, void* variance_bf16, void* stream);
+
+/* Largest closure rank the layout pass folds itself (larger ranks: recap_closure_stats). */
+int recap_gather_max_rank(void);
+
+/* Floats of scratch `workspace` that recap_value_key_covariance needs. */
+int64_t recap_cvk_workspace_floats(int banks, int D, int n_video);
+
+/* Pooled value-key covariance C_vk = sum_t v_t (k_t - kbar_blk(t))^T / n_video on tensor cores,
+ * from the layout pass's v_transposed and k_centred_t.
+ * Replaces pooled_cross_centered_triton_fp32 (recap/kernels/closure_stats.py:245-290).
+ *   cvk [banks, D, D] fp32 out; cvk_bf16 [banks, D, D] bf16 out (nullable). */
+int recap_value_key_covariance(const void* v_transposed, const void* k_centred_t, int banks, int S, int D,
+                               int n_video, float* workspace, float* cvk, void* cvk_bf16, int* status,
+                               void* stream);
 
 /* Top-k block selection.
  * Replaces SparseAttention.head_partition (recap/sparse/attention.py:74-94) with

@@ -16,6 +16,8 @@ import torch
 PACKAGE_DIR = Path(__file__).resolve().parent
 LIB_PATH = PACKAGE_DIR / "librecap_b200.so"
 
+ABI_VERSION = 2  # RECAP_B200_ABI_VERSION of include/recap_b200.h
+
 RECAP_OK = 0
 RECAP_ERR_SHAPE = 1
 RECAP_ERR_LAUNCH = 2
@@ -38,7 +40,11 @@ _F = ctypes.c_float
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "recap_abi_version": (_I, []),
-    "recap_layout_gather": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "recap_layout_gather": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                 _P, _I, _P, _P, _P]),
+    "recap_gather_max_rank": (_I, []),
+    "recap_cvk_workspace_floats": (_I64, [_I, _I, _I]),
+    "recap_value_key_covariance": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "recap_pool_select": (_I, [_P, _P, _I, _I, _I, _I, _F, _I, _I, _P, _P]),
     "recap_partition_overlap": (_I, [_P, _P, _I64, _P, _P]),
     "recap_kernel_block_mask": (_I, [_P, _I, _I, _I, _P, _P]),
@@ -72,6 +78,10 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
+    if lib.recap_abi_version() != ABI_VERSION:
+        raise RuntimeError(
+            f"{target.name} has ABI version {lib.recap_abi_version()}, expected {ABI_VERSION}; rebuild it"
+        )
     _lib = lib
     return lib
 

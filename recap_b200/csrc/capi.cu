@@ -72,7 +72,8 @@ int recap_abi_version(void) { return RECAP_B200_ABI_VERSION; }
 int recap_layout_gather(const void* q, const void* k, const void* v, const int64_t* strides, int batch,
                         int heads, int S, int D, int n_video, const int32_t* src_row, void* q_reordered,
                         void* k_reordered, void* v_transposed, float* q_mean, float* k_mean, float* v_mean,
-                        void* k_mean_bf16, void* v_mean_t_bf16, void* stream) {
+                        void* k_mean_bf16, void* v_mean_t_bf16, void* k_centred_t, const float* basis, int rank,
+                        float* variance, void* variance_bf16, void* stream) {
   Geom g;
   if (!geom(S, n_video, &g) || !d_ok(D) || batch <= 0 || heads <= 0 || strides == nullptr ||
       src_row == nullptr)
@@ -105,7 +106,43 @@ int recap_layout_gather(const void* q, const void* k, const void* v, const int64
   a.mean[2] = v_mean;
   a.kmean_bf16 = static_cast<__nv_bfloat16*>(k_mean_bf16);
   a.vmean_t_bf16 = static_cast<__nv_bfloat16*>(v_mean_t_bf16);
+  a.kct = static_cast<__nv_bfloat16*>(k_centred_t);
+  a.basis = basis;
+  a.rank = rank;
+  a.variance = variance;
+  a.variance_bf16 = static_cast<__nv_bfloat16*>(variance_bf16);
+  if ((a.kct != nullptr || a.variance != nullptr) && k == nullptr) return kErrShape;
   return launch_gather(a, static_cast<cudaStream_t>(stream));
+}
+
+int recap_gather_max_rank(void) { return gather_max_rank(); }
+
+int64_t recap_cvk_workspace_floats(int banks, int D, int n_video) {
+  return static_cast<int64_t>(banks) * cvk_chunks(n_video) * D * D;
+}
+
+int recap_value_key_covariance(const void* v_transposed, const void* k_centred_t, int banks, int S, int D,
+                               int n_video, float* workspace, float* cvk, void* cvk_bf16, int* status,
+                               void* stream) {
+  Geom g;
+  if (!geom(S, n_video, &g) || !d_ok(D) || banks <= 0 || workspace == nullptr || cvk == nullptr)
+    return kErrShape;
+  CvkLaunch L{};
+  L.D = D;
+  int rc = kOk;
+  rc |= make_tmap_bf16(&L.tm_vt, v_transposed, static_cast<uint64_t>(banks) * D, g.S_pad, 128);
+  rc |= make_tmap_bf16(&L.tm_kct, k_centred_t, static_cast<uint64_t>(banks) * D, g.S_pad, D);
+  if (rc != kOk) return kErrShape;
+  L.args.banks = banks;
+  L.args.n_video = n_video;
+  L.args.video_steps = (n_video + 63) / 64;
+  L.args.partial = workspace;
+  L.args.status = status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = launch_cvk(L, s);
+  if (rc != kOk) return rc;
+  return launch_moments_reduce(workspace, banks, cvk_chunks(n_video), D, 1.f / static_cast<float>(n_video), cvk,
+                               static_cast<__nv_bfloat16*>(cvk_bf16), s);
 }
 
 int recap_pool_select(const float* q_mean, const float* k_mean, int banks, int nB, int D, int keep,

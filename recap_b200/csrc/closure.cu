@@ -259,6 +259,13 @@ int launch_closure_variance(const ClosureArgs& a, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
+int launch_moments_reduce(const float* ws, int banks, int nchunks, int D, float inv_n, float* out,
+                          __nv_bfloat16* out_bf16, cudaStream_t s) {
+  dim3 rgrid((D * D + 255) / 256, banks);
+  moments_reduce_kernel<<<rgrid, 256, 0, s>>>(ws, nchunks, D, inv_n, out, out_bf16);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
 int launch_basis_prep(const BasisPrepArgs& a, cudaStream_t s) {
   dim3 grid((a.D * a.D + 255) / 256, a.banks);
   basis_prep_kernel<<<grid, 256, 0, s>>>(a);

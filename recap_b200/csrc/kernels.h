@@ -32,8 +32,30 @@ struct GatherArgs {
   float* mean[3];               // [banks, nB, D] block means over video tokens (nullable each)
   __nv_bfloat16* kmean_bf16;    // [banks, nB_pad, D] (nullable)
   __nv_bfloat16* vmean_t_bf16;  // [banks, D, nB_pad] (nullable)
+  __nv_bfloat16* kct;           // [banks, D, S_pad] block-centred video keys, transposed (nullable)
+  const float* basis;           // [banks, D, D] fp32 (with variance)
+  int rank;                     // 0 < rank < D, rank <= gather_max_rank()
+  float* variance;              // [banks, nB, D] rank-folded per-block variance in the basis (nullable)
+  __nv_bfloat16* variance_bf16; // [banks, nB_pad, D] (nullable)
 };
 int launch_gather(const GatherArgs& a, cudaStream_t s);
+int gather_max_rank();
+
+// ------------------------------------------------------------------ C_vk on tensor cores
+struct CvkArgs {
+  int banks, n_video, video_steps;  // video_steps = ceil(n_video / 64)
+  float* partial;                   // [banks, cvk_chunks, D, D]
+  int* status;
+};
+struct CvkLaunch {
+  int D;
+  CUtensorMap tm_vt, tm_kct;
+  CvkArgs args;
+};
+int cvk_chunks(int n_video);
+int launch_cvk(const CvkLaunch& L, cudaStream_t s);
+int launch_moments_reduce(const float* ws, int banks, int nchunks, int D, float inv_n, float* out,
+                          __nv_bfloat16* out_bf16, cudaStream_t s);
 
 // ------------------------------------------------------------------ selection
 struct SelectArgs {

@@ -1,20 +1,28 @@
-// Layout gather fused with block pooling.
+// Layout gather fused with block pooling and the per-call closure statistics of K.
 //
-// One pass over the native-order Q, K and V of a layer call:
+// One pass over the native-order Q, K and V of a layer call, one CTA per 128-token block:
 //  * reorders the tokens into [Hilbert-ordered video | text] (Layout.reorder,
 //    recap/sparse/layout.py:86-90), writing Q and K as [banks, S_pad, D] and V
 //    transposed as [banks, D, S_pad] (the K-major operand layout of P V);
-//  * sums each 128-token block over its video tokens in fp32 and divides by the
-//    block's token count (pool_blocks, recap/sparse/pooling.py:10-34), writing
-//    the fp32 means and the bf16 copies the coarse tail reads.
-// Rows past S (up to S_pad) are written as zeros.  HBM-bound: every input byte
-// is read once and every output byte written once.
+//  * sums each block over its video tokens in fp32 and divides by the token count
+//    (pool_blocks, recap/sparse/pooling.py:10-34): fp32 means plus the bf16 copies the
+//    coarse tail reads;
+//  * writes the block-centred video keys k - kbar, transposed and rounded to bf16, as
+//    the K-major B operand of the C_vk GEMM (recap/kernels/closure_stats.py:27-94);
+//  * with a basis U and 0 < rank < D, the rank-folded per-block key variances in U
+//    (rotated_leaf_moments_triton + fold_rank, recap/kernels/closure_stats.py:96-189,
+//    recap/sparse/closure.py:96-104): the leading `rank` columns are the two-pass
+//    population variances of K U[:, c]; every other column is their mean, which for an
+//    orthonormal U equals (trace of the block covariance - the leading variances) /
+//    (D - rank), so only K U[:, :rank] is formed.
+// Rows past S (up to S_pad) are written as zeros.  HBM-bound.
 #include "kernels.h"
 
 namespace recap {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kMaxRank = 8;
 
 __device__ __forceinline__ void add8(float (&acc)[8], const uint4& w) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
@@ -27,13 +35,31 @@ __device__ __forceinline__ void add8(float (&acc)[8], const uint4& w) {
 }
 
 template <int D>
+struct GatherSmem {
+  static constexpr int VSTRIDE = D + 8;  // padded bf16 row of a staged tile
+  static constexpr int kV = 0;
+  static constexpr int kK = kV + 128 * VSTRIDE * 2;
+  static constexpr int kRed = kK + 128 * VSTRIDE * 2;        // [RPP][D] fp32
+  static constexpr int kMean = kRed + 32 * D * 4;            // [D] fp32 key means
+  static constexpr int kRot = kMean + D * 4;                 // [128][kMaxRank] fp32
+  static constexpr int kStat = kRot + 128 * kMaxRank * 4;    // [2*kMaxRank + 1]
+  static constexpr int kTotal = kStat + 64 * 4;
+};
+
+template <int D>
 __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
+  using L = GatherSmem<D>;
   constexpr int CPR = D / 8;              // 16-byte chunks per row
   constexpr int RPP = kThreads / CPR;     // rows per pass
   constexpr int PASSES = 128 / RPP;
-  constexpr int VSTRIDE = D + 8;          // padded row of the staged V tile
-  __shared__ __align__(16) __nv_bfloat16 vtile[128 * VSTRIDE];
-  __shared__ float red[RPP * D];
+  constexpr int VSTRIDE = L::VSTRIDE;
+  extern __shared__ __align__(16) uint8_t smem[];
+  __nv_bfloat16* vtile = reinterpret_cast<__nv_bfloat16*>(smem + L::kV);
+  __nv_bfloat16* ktile = reinterpret_cast<__nv_bfloat16*>(smem + L::kK);
+  float* red = reinterpret_cast<float*>(smem + L::kRed);
+  float* kmean_s = reinterpret_cast<float*>(smem + L::kMean);
+  float* rot = reinterpret_cast<float*>(smem + L::kRot);
+  float* stat = reinterpret_cast<float*>(smem + L::kStat);
 
   const int blk = blockIdx.x;
   const int bank = blockIdx.y;
@@ -44,6 +70,7 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
   const int rsub = tid / CPR;
   const int row0 = blk * 128;
   const int video_rows = min(128, a.n_video - row0);  // <= 0 for text-only blocks
+  const bool need_k_tile = (a.kct != nullptr || a.variance != nullptr) && video_rows > 0;
 
   for (int t = 0; t < 3; ++t) {
     const __nv_bfloat16* src = a.src[t];
@@ -64,14 +91,17 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
       }
       if (t == 0 && a.qr) {
         *reinterpret_cast<uint4*>(a.qr + (static_cast<size_t>(bank) * a.S_pad + r) * D + ch * 8) = val;
-      } else if (t == 1 && a.kr) {
-        *reinterpret_cast<uint4*>(a.kr + (static_cast<size_t>(bank) * a.S_pad + r) * D + ch * 8) = val;
+      } else if (t == 1) {
+        if (a.kr)
+          *reinterpret_cast<uint4*>(a.kr + (static_cast<size_t>(bank) * a.S_pad + r) * D + ch * 8) = val;
+        if (need_k_tile) *reinterpret_cast<uint4*>(ktile + rl * VSTRIDE + ch * 8) = val;
       } else if (t == 2) {
         *reinterpret_cast<uint4*>(vtile + rl * VSTRIDE + ch * 8) = val;
       }
       if (rl < video_rows) add8(acc, val);
     }
-    if (a.mean[t] != nullptr && blk < a.nB) {
+    const bool want_mean = blk < a.nB && (a.mean[t] != nullptr || (t == 1 && need_k_tile));
+    if (want_mean) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) red[rsub * D + ch * 8 + e] = acc[e];
       __syncthreads();
@@ -80,7 +110,8 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
 #pragma unroll 4
         for (int g = 0; g < RPP; ++g) s += red[g * D + tid];
         const float m = s / static_cast<float>(video_rows);
-        a.mean[t][(static_cast<size_t>(bank) * a.nB + blk) * D + tid] = m;
+        if (t == 1) kmean_s[tid] = m;
+        if (a.mean[t]) a.mean[t][(static_cast<size_t>(bank) * a.nB + blk) * D + tid] = m;
         if (t == 1 && a.kmean_bf16)
           a.kmean_bf16[(static_cast<size_t>(bank) * a.nB_pad + blk) * D + tid] = __float2bfloat16_rn(m);
         if (t == 2 && a.vmean_t_bf16)
@@ -89,8 +120,8 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
       __syncthreads();
     }
   }
+
   if (a.vt != nullptr && a.src[2] != nullptr) {
-    __syncthreads();
     // transposed write: lanes run over d so that the staged reads are conflict-free
     for (int idx = tid; idx < D * 16; idx += kThreads) {
       const int d = idx % D;
@@ -107,20 +138,106 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
           make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
+
+  if (a.kct != nullptr) {
+    // centred video keys, transposed, bf16; zero outside the video tokens
+    for (int idx = tid; idx < D * 16; idx += kThreads) {
+      const int d = idx % D;
+      const int kc = idx / D;
+      const float m = video_rows > 0 ? kmean_s[d] : 0.f;
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r0 = kc * 8 + 2 * e;
+        const float x0 = r0 < video_rows ? __bfloat162float(ktile[r0 * VSTRIDE + d]) - m : 0.f;
+        const float x1 = r0 + 1 < video_rows ? __bfloat162float(ktile[(r0 + 1) * VSTRIDE + d]) - m : 0.f;
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        w[e] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(a.kct + (static_cast<size_t>(bank) * D + d) * a.S_pad + row0 + kc * 8) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+
+  if (a.variance != nullptr && blk < a.nB && video_rows > 0) {
+    const int rank = a.rank;
+    const float* U = a.basis + static_cast<size_t>(bank) * D * D;
+    // rotated values of the leading columns: rot[r][c] = sum_d k[r][d] U[d][c]
+    for (int idx = tid; idx < 128 * rank; idx += kThreads) {
+      const int r = idx / rank;
+      const int c = idx % rank;
+      float s = 0.f;
+      if (r < video_rows) {
+#pragma unroll 8
+        for (int d = 0; d < D; ++d) s = fmaf(__bfloat162float(ktile[r * VSTRIDE + d]), U[d * D + c], s);
+      }
+      rot[r * kMaxRank + c] = s;
+    }
+    // per-dimension squared deviations for the trace of the block covariance
+    float tr = 0.f;
+    if (tid < D) {
+      const float m = kmean_s[tid];
+      for (int r = 0; r < video_rows; ++r) {
+        const float x = __bfloat162float(ktile[r * VSTRIDE + tid]) - m;
+        tr = fmaf(x, x, tr);
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) tr += __shfl_xor_sync(0xffffffffu, tr, o);
+    if ((tid & 31) == 0 && tid < D) red[tid >> 5] = tr;
+    __syncthreads();
+    if (tid < rank) {
+      // two-pass population variance of column tid of K U
+      float s = 0.f;
+      for (int r = 0; r < video_rows; ++r) s += rot[r * kMaxRank + tid];
+      const float m = s / static_cast<float>(video_rows);
+      float ss = 0.f;
+      for (int r = 0; r < video_rows; ++r) {
+        const float x = rot[r * kMaxRank + tid] - m;
+        ss = fmaf(x, x, ss);
+      }
+      stat[tid] = fmaxf(ss / static_cast<float>(video_rows), 0.f);
+    }
+    __syncthreads();
+    if (tid < D) {
+      float v;
+      if (tid < rank) {
+        v = stat[tid];
+      } else {
+        float total = 0.f;
+        for (int q = 0; q < D / 32; ++q) total += red[q];
+        total /= static_cast<float>(video_rows);
+        float lead = 0.f;
+        for (int c = 0; c < rank; ++c) lead += stat[c];
+        v = fmaxf(total - lead, 0.f) / static_cast<float>(D - rank);
+      }
+      a.variance[(static_cast<size_t>(bank) * a.nB + blk) * D + tid] = v;
+      if (a.variance_bf16)
+        a.variance_bf16[(static_cast<size_t>(bank) * a.nB_pad + blk) * D + tid] = __float2bfloat16_rn(v);
+    }
+  }
 }
 
 }  // namespace
 
 int launch_gather(const GatherArgs& a, cudaStream_t s) {
   if (a.S_pad % 128 || a.S > a.S_pad || a.n_video > a.S || a.n_video <= 0) return kErrShape;
-  dim3 grid(a.S_pad / 128, a.batch * a.heads);
-  if (a.D == 128)
-    gather_kernel<128><<<grid, kThreads, 0, s>>>(a);
-  else if (a.D == 64)
-    gather_kernel<64><<<grid, kThreads, 0, s>>>(a);
-  else
+  if (a.variance != nullptr && (a.basis == nullptr || a.rank <= 0 || a.rank >= a.D || a.rank > kMaxRank))
     return kErrShape;
+  dim3 grid(a.S_pad / 128, a.batch * a.heads);
+  if (a.D == 128) {
+    const int smem = GatherSmem<128>::kTotal;
+    cudaFuncSetAttribute(gather_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    gather_kernel<128><<<grid, kThreads, smem, s>>>(a);
+  } else if (a.D == 64) {
+    const int smem = GatherSmem<64>::kTotal;
+    cudaFuncSetAttribute(gather_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    gather_kernel<64><<<grid, kThreads, smem, s>>>(a);
+  } else {
+    return kErrShape;
+  }
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
+
+int gather_max_rank() { return kMaxRank; }
 
 }  // namespace recap

@@ -107,6 +107,9 @@ class LayerInputs:
     v_mean: torch.Tensor | None
     k_mean_bf16: torch.Tensor | None  # [banks, nB_pad, D]
     v_mean_t_bf16: torch.Tensor | None  # [banks, D, nB_pad]
+    k_centred_t: torch.Tensor | None = None  # [banks, D, S_pad] bf16, block-centred video keys
+    variance: torch.Tensor | None = None  # [banks, nB, D] fp32 rank-folded (when the basis was known)
+    variance_bf16: torch.Tensor | None = None  # [banks, nB_pad, D]
 
 
 class Launches:
@@ -183,7 +186,9 @@ class SparseAttention:
         q_r = torch.empty(sh.banks, sh.S_pad, sh.D, dtype=bf, device=dev)
         k_r = torch.empty_like(q_r)
         v_t = torch.empty(sh.banks, sh.D, sh.S_pad, dtype=bf, device=dev)
-        qm = km = vm = kmb = vmtb = None
+        qm = km = vm = kmb = vmtb = kct = var = var_bf16 = None
+        basis = None
+        rank = int(self.config.closure_rank)
         if means:
             f32 = torch.float32
             km = torch.empty(sh.banks, sh.nB, sh.D, dtype=f32, device=dev)
@@ -191,15 +196,22 @@ class SparseAttention:
             qm = torch.empty_like(km) if q_mean else None
             kmb = torch.zeros(sh.banks, sh.nB_pad, sh.D, dtype=bf, device=dev)
             vmtb = torch.zeros(sh.banks, sh.D, sh.nB_pad, dtype=bf, device=dev)
+            kct = torch.empty(sh.banks, sh.D, sh.S_pad, dtype=bf, device=dev)
+            if (self._basis is not None and 0 < rank < sh.D and rank <= _lib.load().recap_gather_max_rank()
+                    and self._basis.shape == (sh.banks, sh.D, sh.D)):
+                basis = self._basis
+                var = torch.empty(sh.banks, sh.nB, sh.D, dtype=f32, device=dev)
+                var_bf16 = torch.zeros(sh.banks, sh.nB_pad, sh.D, dtype=bf, device=dev)
         strides = _strides3(query, key, value)
         self.launches.run(
             "recap_layout_gather", 1,
             _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), strides,
             sh.batch, sh.heads, sh.S, sh.D, sh.n_video, _lib.ptr(gather_rows(layout, dev)),
             _lib.ptr(q_r), _lib.ptr(k_r), _lib.ptr(v_t), _lib.ptr(qm), _lib.ptr(km), _lib.ptr(vm),
-            _lib.ptr(kmb), _lib.ptr(vmtb), _lib.stream_handle(dev),
+            _lib.ptr(kmb), _lib.ptr(vmtb), _lib.ptr(kct), _lib.ptr(basis), rank if basis is not None else 0,
+            _lib.ptr(var), _lib.ptr(var_bf16), _lib.stream_handle(dev),
         )
-        return LayerInputs(sh, q_r, k_r, v_t, qm, km, vm, kmb, vmtb)
+        return LayerInputs(sh, q_r, k_r, v_t, qm, km, vm, kmb, vmtb, kct, var, var_bf16)
 
     # -- the partition --------------------------------------------------------------------
 
@@ -223,44 +235,53 @@ class SparseAttention:
     @torch.no_grad()
     def coarse_tail_context(self, inputs: LayerInputs, scale: float) -> dict:
         """Closure statistics that do not depend on the partition
-        (recap/sparse/attention.py:98-202)."""
+        (recap/sparse/attention.py:98-202): C_vk on tensor cores every call; the basis at
+        the first call of a sample (scatter, eigh, ordering by pooled variance); the
+        rank-folded per-block variances (from the layout pass when the basis was known)."""
         sh = inputs.shapes
         dev = inputs.q.device
         f32 = torch.float32
         rank = int(self.config.closure_rank)
-        ws = torch.empty(
-            int(_lib.load().recap_closure_workspace_floats(sh.banks, sh.D, sh.n_video)),
-            dtype=f32, device=dev,
-        )
+        stream = _lib.stream_handle(dev)
+        lib = _lib.load()
+        if inputs.k_centred_t is None:
+            raise ValueError("coarse_tail_context needs the layout pass's block means and centred keys")
+        ws = torch.empty(int(lib.recap_cvk_workspace_floats(sh.banks, sh.D, sh.n_video)), dtype=f32, device=dev)
         cvk = torch.empty(sh.banks, sh.D, sh.D, dtype=f32, device=dev)
         cvk_bf16 = torch.empty(sh.banks, sh.D, sh.D, dtype=torch.bfloat16, device=dev)
-        variance = torch.empty(sh.banks, sh.nB, sh.D, dtype=f32, device=dev)
-        variance_bf16 = torch.zeros(sh.banks, sh.nB_pad, sh.D, dtype=torch.bfloat16, device=dev)
-        stream = _lib.stream_handle(dev)
+        self.launches.run(
+            "recap_value_key_covariance", 2, _lib.ptr(inputs.v_t), _lib.ptr(inputs.k_centred_t), sh.banks, sh.S,
+            sh.D, sh.n_video, _lib.ptr(ws), _lib.ptr(cvk), _lib.ptr(cvk_bf16), None, stream,
+        )
+        variance, variance_bf16 = inputs.variance, inputs.variance_bf16
 
-        def closure(basis, scatter, want_cvk, out_var, out_var_bf16, fold):
-            n = 0
-            if scatter is not None or want_cvk:
-                n += 1 + (scatter is not None) + bool(want_cvk)
-            if basis is not None:
-                n += 1
+        def full_variance(basis, fold):
+            """Per-block variances of every basis column (the first call's ordering needs
+            them all), folded to `fold` (0: not folded)."""
+            out = torch.empty(sh.banks, sh.nB, sh.D, dtype=f32, device=dev)
+            out_bf16 = torch.zeros(sh.banks, sh.nB_pad, sh.D, dtype=torch.bfloat16, device=dev)
             self.launches.run(
-                "recap_closure_stats", n,
+                "recap_closure_stats", 1,
                 _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(inputs.k_mean), sh.banks, sh.S, sh.D,
-                sh.n_video, fold, _lib.ptr(basis), _lib.ptr(scatter),
-                _lib.ptr(cvk) if want_cvk else None, _lib.ptr(cvk_bf16) if want_cvk else None,
-                _lib.ptr(out_var), _lib.ptr(out_var_bf16), _lib.ptr(ws), stream,
+                sh.n_video, fold, _lib.ptr(basis), None, None, None, _lib.ptr(out), _lib.ptr(out_bf16), None,
+                stream,
             )
+            return out, out_bf16
 
         if self._basis is None:
             # first call of the sample: scatter -> eigenbasis -> order by pooled variance
             scatter = torch.empty(sh.banks, sh.D, sh.D, dtype=f32, device=dev)
-            closure(None, scatter, True, None, None, 0)
+            sws = torch.empty(int(lib.recap_closure_workspace_floats(sh.banks, sh.D, sh.n_video)), dtype=f32,
+                              device=dev)
+            self.launches.run(
+                "recap_closure_stats", 2,
+                _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(inputs.k_mean), sh.banks, sh.S, sh.D,
+                sh.n_video, 0, None, _lib.ptr(scatter), None, None, None, None, _lib.ptr(sws), stream,
+            )
             symmetric = 0.5 * (scatter + scatter.transpose(-1, -2))
             _, evecs = torch.linalg.eigh(symmetric)
             evecs = evecs.contiguous()
-            unsorted = torch.empty_like(variance)
-            closure(evecs, None, False, unsorted, None, 0)
+            unsorted, _ = full_variance(evecs, 0)
             counts = self.geometry.block_counts.to(dev).reshape(1, -1, 1)
             pooled = (unsorted * counts).sum(1) / counts.sum().clamp_min(1.0)
             order = torch.argsort(pooled, dim=-1, descending=True)
@@ -268,11 +289,12 @@ class SparseAttention:
             basis_t = torch.empty(sh.banks, sh.D, sh.D, dtype=torch.bfloat16, device=dev)
             self.launches.run("recap_basis_prep", 1, _lib.ptr(basis), sh.banks, sh.D, _lib.ptr(basis_t), stream)
             self._basis, self._basis_t = basis, basis_t
-            closure(basis, None, False, variance, variance_bf16, rank)
+            variance, variance_bf16 = full_variance(basis, rank)
         else:
             if self._basis.shape[0] != sh.banks or self._basis.shape[-1] != sh.D:
                 raise ValueError("cached basis does not match this call's banks/head_dim")
-            closure(self._basis, None, True, variance, variance_bf16, rank)
+            if variance is None:
+                variance, variance_bf16 = full_variance(self._basis, rank)
         return {
             "variance": variance, "variance_bf16": variance_bf16, "cvk": cvk, "cvk_bf16": cvk_bf16,
             "basis": self._basis, "basis_t": self._basis_t,

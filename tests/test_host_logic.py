@@ -86,7 +86,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), name
     assert set(declared) == set(_lib.SIGNATURES), "ctypes signatures must cover the header"
-    assert _lib.load().recap_abi_version() == 1
+    assert _lib.load().recap_abi_version() == _lib.ABI_VERSION
 
 
 def test_library_rejects_bad_shapes_without_a_gpu():
