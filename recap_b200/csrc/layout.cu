@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
     }
   }
 
+  __syncthreads();  // the staged V and K tiles are complete before anyone reads them back
   if (a.vt != nullptr && a.src[2] != nullptr) {
     // transposed write: lanes run over d so that the staged reads are conflict-free
     for (int idx = tid; idx < D * 16; idx += kThreads) {

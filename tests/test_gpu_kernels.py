@@ -220,6 +220,9 @@ def test_closure_statistics_vs_oracle(d, nv, text, text_first):
     cvk = orc.cross_covariance(k_r, v_r, km, counts, nv)
     err = (ctx["cvk"].cpu() - cvk).abs().max().item()
     assert err <= 2e-3 * max(1.0, float(cvk.abs().max())), err
+    basis = ctx["basis"].cpu()
+    var = orc.fold_rank(orc.rotated_variance(k_r, basis, nv), 4)
+    assert torch.allclose(ctx["variance"].cpu(), var, atol=1e-4, rtol=1e-3), (ctx["variance"].cpu() - var).abs().max()
     # the basis is an ordered eigenbasis of the pooled within-block scatter
     scat = orc.within_block_scatter(k_r, km, counts, nv)
     evals = torch.linalg.eigvalsh(scat.double())
