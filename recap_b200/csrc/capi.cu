@@ -222,8 +222,8 @@ int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const v
   rc |= make_tmap_bf16(&L.tm_q, q_reordered, static_cast<uint64_t>(banks) * g.S_pad, D, 128);
   rc |= make_tmap_bf16(&L.tm_basis_t, basis_t_bf16, static_cast<uint64_t>(banks) * D, D, D);
   rc |= make_tmap_bf16(&L.tm_cvk, cvk_bf16, static_cast<uint64_t>(banks) * D, D, D);
-  rc |= make_tmap_bf16(&L.tm_kmean, k_mean_bf16, static_cast<uint64_t>(banks) * g.nB_pad, D, 128);
-  rc |= make_tmap_bf16(&L.tm_var, variance_bf16, static_cast<uint64_t>(banks) * g.nB_pad, D, 128);
+  rc |= make_tmap_bf16(&L.tm_kmean, k_mean_bf16, static_cast<uint64_t>(banks) * g.nB_pad, D, 64);
+  rc |= make_tmap_bf16(&L.tm_var, variance_bf16, static_cast<uint64_t>(banks) * g.nB_pad, D, 64);
   rc |= make_tmap_bf16(&L.tm_vmean_t, v_mean_t_bf16, static_cast<uint64_t>(banks) * D, g.nB_pad, D);
   if (rc != kOk) return kErrShape;
   CoarseArgs& a = L.args;

@@ -163,17 +163,46 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
   if (a.variance != nullptr && blk < a.nB && video_rows > 0) {
     const int rank = a.rank;
     const float* U = a.basis + static_cast<size_t>(bank) * D * D;
-    // rotated values of the leading columns: rot[r][c] = sum_d k[r][d] U[d][c]
-    for (int idx = tid; idx < 128 * rank; idx += kThreads) {
-      const int r = idx / rank;
-      const int c = idx % rank;
-      float s = 0.f;
-      if (r < video_rows) {
-#pragma unroll 8
-        for (int d = 0; d < D; ++d) s = fmaf(__bfloat162float(ktile[r * VSTRIDE + d]), U[d * D + c], s);
-      }
-      rot[r * kMaxRank + c] = s;
+    // leading basis columns, staged as us[c][d] (read as broadcasts below)
+    float* us = red;  // the pooling scratch is free here: [kMaxRank][D] fits in [32][D]
+    for (int idx = tid; idx < rank * D; idx += kThreads) {
+      const int c = idx / D;
+      const int d = idx % D;
+      us[c * D + d] = U[d * D + c];
     }
+    __syncthreads();
+    // rotated values of the leading columns, one key row per thread:
+    // rot[r][c] = sum_d k[r][d] U[d][c]
+    if (tid < 128) {
+      const int r = tid;
+      float acc[kMaxRank];
+#pragma unroll
+      for (int c = 0; c < kMaxRank; ++c) acc[c] = 0.f;
+      if (r < video_rows) {
+#pragma unroll 4
+        for (int j = 0; j < D / 8; ++j) {
+          const uint4 w = *reinterpret_cast<const uint4*>(ktile + r * VSTRIDE + j * 8);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+          float x[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            x[2 * e] = f.x;
+            x[2 * e + 1] = f.y;
+          }
+#pragma unroll
+          for (int c = 0; c < kMaxRank; ++c) {
+            if (c < rank) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc[c] = fmaf(x[e], us[c * D + j * 8 + e], acc[c]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kMaxRank; ++c) rot[r * kMaxRank + c] = acc[c];
+    }
+    __syncthreads();  // us (in red) is read before red takes the trace partial sums
     // per-dimension squared deviations for the trace of the block covariance
     float tr = 0.f;
     if (tid < D) {
