@@ -304,9 +304,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bars.sfree + b);
-      float mx = -INFINITY;
+      float mxa[8];
 #pragma unroll
-      for (int i = 0; i < kTileN; ++i) mx = fmaxf(mx, x[i]);
+      for (int k = 0; k < 8; ++k) mxa[k] = x[k];
+#pragma unroll
+      for (int i = 8; i < kTileN; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], x[i]);
+      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
       float alpha = 1.f;
       bool rescale = false;
       if (mx != -INFINITY) {
@@ -318,17 +322,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           rescale = true;
         }
       }
-      float lsum = 0.f, gsum = 0.f;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f}, gs[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[kTileN / 2];
 #pragma unroll
       for (int e = 0; e < kTileN / 2; ++e) {
         const int c0 = 2 * e, c1 = 2 * e + 1;
         const float p0 = x[c0] == -INFINITY ? 0.f : fast_exp2(x[c0] - m_run);
         const float p1 = x[c1] == -INFINITY ? 0.f : fast_exp2(x[c1] - m_run);
-        lsum += p0 + p1;
-        gsum += (((gate[c0 >> 5] >> (c0 & 31)) & 1u) ? p0 : 0.f) + (((gate[c1 >> 5] >> (c1 & 31)) & 1u) ? p1 : 0.f);
+        ls[e & 3] += p0 + p1;
+        gs[e & 3] += (((gate[c0 >> 5] >> (c0 & 31)) & 1u) ? p0 : 0.f) + (((gate[c1 >> 5] >> (c1 & 31)) & 1u) ? p1 : 0.f);
         pk[e] = pack_bf16(p0, p1);
       }
+      const float lsum = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      const float gsum = (gs[0] + gs[1]) + (gs[2] + gs[3]);
       l_run = l_run * alpha + lsum;
       g_run = g_run * alpha + gsum;
       if (j > 0) {
