@@ -281,4 +281,9 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 
 __device__ __forceinline__ int elect_lane0() { return (threadIdx.x & 31) == 0; }
 
+// Named barrier among `count` threads (a multiple of 32) of the CTA; id 0 is __syncthreads.
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 }  // namespace recap

@@ -4,14 +4,18 @@
 // call of recap/kernels/block_sparse.py:78-139 and the dense flash call of
 // recap/operator.py:254-256 (the same kernel run with every key block kept).
 //
-// One CTA per (bank, query block); 8 warps:
+// One CTA per (bank, query block); 12 warps:
 //   warp 0      TMA producer: the Q tile once, then K and V^T tiles of every kept
 //               key block through a ring of NST shared-memory slots;
 //   warp 1      TMEM allocator and MMA issuer (one thread): S = Q K^T into one of
 //               two TMEM S buffers, O += P V into the TMEM O accumulator;
-//   warps 4-7   softmax warpgroup, one query row per thread (TMEM lane = row):
-//               online softmax in the log2 domain with lazy rescaling of O, P
-//               written as bf16 to shared memory, then the epilogue.
+//   warps 4-11  softmax, two warpgroups per query tile: each query row is shared by
+//               one thread of each group (TMEM lane = row), group g taking key columns
+//               [64g, 64g + 64) of S and output columns [D/2 g, D/2 (g+1)).  The groups
+//               exchange row maxima each tile, so both rescale with the same running
+//               max (log2 domain, lazy rescaling of O), write their half of P as bf16 to
+//               shared memory, and split the epilogue.  Two softmax warps per SM
+//               sub-partition hide each other's latency.
 // The epilogue either writes O (bf16) and LSE, or applies the corrected merge of
 // recap/kernels/detail_cache.py:188-301 (drift-weighted refinement + coarse
 // tail, merged in log-mass space) and writes the result straight to the native
@@ -23,7 +27,7 @@ namespace recap {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
 constexpr int kSoftmaxWarp0 = 4;
 constexpr int kMaxKeyBlocks = 2048;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when max grows by 2^8
@@ -36,11 +40,13 @@ struct FmhaSmem {
   static constexpr int kP = kQ + kTileBytes;
   static constexpr int kKV = kP + 128 * 128 * 2;
   static constexpr int kBars = kKV + kNst * kTileBytes;
-  // barriers: qfull, full[NST], empty[NST], sfull[2], sfree[2], pfull, ofull, done
-  static constexpr int kNumBars = 1 + 2 * kNst + 2 + 2 + 3;
+  // barriers: qfull, full[NST], empty[NST], sfull[2], sfree[2], pfull, ofull, done, xchg[2], xsum
+  static constexpr int kNumBars = 1 + 2 * kNst + 2 + 2 + 3 + 3;
   static constexpr int kMisc = kBars + kNumBars * 8;  // tmem addr, abort flag, list length
   static constexpr int kList = kMisc + 16;
-  static constexpr int kTotal = kList + kMaxKeyBlocks * 4;
+  static constexpr int kRowMax = kList + kMaxKeyBlocks * 4;  // [2 parity][2 halves][128] fp32
+  static constexpr int kRowSum = kRowMax + 2 * 2 * 128 * 4;  // [2 halves][128] fp32
+  static constexpr int kTotal = kRowSum + 2 * 128 * 4;
 };
 
 struct Bars {
@@ -52,6 +58,8 @@ struct Bars {
   uint64_t* pfull;
   uint64_t* ofull;
   uint64_t* done;
+  uint64_t* xchg;  // [2] row-max exchange between the two softmax warpgroups, by tile parity
+  uint64_t* xsum;  // row-sum exchange at the end
 };
 
 template <int NST>
@@ -66,6 +74,8 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* base) {
   r.pfull = b + 5 + 2 * NST;
   r.ofull = b + 6 + 2 * NST;
   r.done = b + 7 + 2 * NST;
+  r.xchg = b + 8 + 2 * NST;
+  r.xsum = b + 10 + 2 * NST;
   return r;
 }
 
@@ -88,6 +98,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
   int* list_len = reinterpret_cast<int*>(smem + L::kMisc + 8);
   int* list = reinterpret_cast<int*>(smem + L::kList);
+  float* rowmax = reinterpret_cast<float*>(smem + L::kRowMax);
+  float* rowsum = reinterpret_cast<float*>(smem + L::kRowSum);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -110,11 +122,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bars.sfull + b, 1);
-      mbar_init(bars.sfree + b, 4);
+      mbar_init(bars.sfree + b, 8);  // both softmax warpgroups read each S buffer
     }
-    mbar_init(bars.pfull, 4);
+    mbar_init(bars.pfull, 8);
     mbar_init(bars.ofull, 1);
     mbar_init(bars.done, 1);
+    mbar_init(bars.xchg, 8);
+    mbar_init(bars.xchg + 1, 8);
+    mbar_init(bars.xsum, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -244,12 +259,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kSoftmaxWarp0) {
     // ================================================================ softmax + epilogue
-    const int t = threadIdx.x - kSoftmaxWarp0 * 32;  // query row within the block
-    const uint32_t lane_base = static_cast<uint32_t>((warp - kSoftmaxWarp0) * 32) << 16;
+    // Two warpgroups share every query row: group g handles key columns [64g, 64g + 64)
+    // of S and output columns [D/2 g, D/2 (g + 1)); the row max is exchanged through
+    // shared memory each tile so both groups use the same running max.
+    const int g = (warp - kSoftmaxWarp0) >> 2;   // column half
+    const int q4 = (warp - kSoftmaxWarp0) & 3;   // TMEM lane quarter
+    const int t = q4 * 32 + lane;                // query row within the block
+    const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
     const float scale_log2 = args.scale_log2;
-    float m_run = -INFINITY;  // running max, log2 domain (scaled)
-    float l_run = 0.f;
-    const uint32_t p_row = smem_u32(sP) + t * 128;
+    float m_run = -INFINITY;  // running max, log2 domain (scaled), identical in both groups
+    float l_run = 0.f;        // this group's share of the row sum
+    const uint32_t p_row = smem_u32(sP) + g * 16384 + t * 128;  // P columns [64g, 64g + 64)
     bool ok = n_kv > 0;
     for (int j = 0; ok && j < n_kv; ++j) {
       const int b = j & 1;
@@ -257,11 +277,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      float x[128];
+      float x[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float v[32];
-        tmem_ld32(t_s + b * 128 + c * 32 + lane_base, v);
+        tmem_ld32(t_s + b * 128 + g * 64 + c * 32 + lane_base, v);
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i];
       }
@@ -270,22 +290,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bars.sfree + b);
       // keys past the end of the sequence (last, partial key block)
-      const int blk = list[j];
-      const int valid = args.S - blk * 128;
-      if (valid < 128) {
+      const int valid = args.S - list[j] * 128 - g * 64;
+      if (valid < 64) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
+        for (int i = 0; i < 64; ++i)
           if (i >= valid) x[i] = -INFINITY;
       }
-      // row max with 8 independent partial maxima (a serial chain of 128 would leave the
-      // single softmax warp of each SM sub-partition waiting on its own latency)
       float mxa[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) mxa[k] = x[k];
 #pragma unroll
-      for (int i = 8; i < 128; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], x[i]);
-      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+      for (int i = 8; i < 64; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], x[i]);
+      float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                       fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+      // exchange the half-row maxima (double-buffered by tile parity); an mbarrier with a
+      // bounded wait, so that a warpgroup that aborts cannot strand the other one
+      rowmax[(b * 2 + g) * 128 + t] = mx;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars.xchg + b);
+      ok = mbar_wait(bars.xchg + b, (j >> 1) & 1, abort_flag, args.status, kStatusTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      mx = fmaxf(mx, rowmax[(b * 2 + (g ^ 1)) * 128 + t]);
       const float m_tile = mx * scale_log2;
       float alpha = 1.f;
       bool rescale = false;
@@ -296,20 +322,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_run = m_tile;
         rescale = true;
       }
-      float sa[8];
+      float sa[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[32];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) sa[k] = 0.f;
-      uint32_t pk[64];
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
+      for (int i = 0; i < 32; ++i) {
         const float p0 = fast_exp2(fmaf(x[2 * i], scale_log2, -m_run));
         const float p1 = fast_exp2(fmaf(x[2 * i + 1], scale_log2, -m_run));
-        sa[(2 * i) & 7] += p0;
-        sa[(2 * i + 1) & 7] += p1;
+        sa[i & 3] += p0 + p1;
         pk[i] = pack_bf16(p0, p1);
       }
-      const float sum = ((sa[0] + sa[1]) + (sa[2] + sa[3])) + ((sa[4] + sa[5]) + (sa[6] + sa[7]));
-      l_run = l_run * alpha + sum;
+      l_run = l_run * alpha + ((sa[0] + sa[1]) + (sa[2] + sa[3]));
       // PV(j-1) must be complete before P is overwritten and O is rescaled.
       if (j > 0) {
         ok = mbar_wait(bars.ofull, (j - 1) & 1, abort_flag, args.status, kStatusTimeoutSoftmax);
@@ -318,24 +340,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < D / 64; ++c) {
             float v[32];
-            tmem_ld32(t_o + c * 32 + lane_base, v);
+            const uint32_t col = t_o + g * (D / 2) + c * 32 + lane_base;
+            tmem_ld32(col, v);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= alpha;
-            tmem_st32(t_o + c * 32 + lane_base, v);
+            tmem_st32(col, v);
           }
           tmem_wait_st();
         }
       }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const int atom = c >> 3;
-        const int cc = c & 7;
-        st_shared_v4(p_row + atom * 16384 + ((cc ^ (t & 7)) << 4), pk[4 * c], pk[4 * c + 1],
-                     pk[4 * c + 2], pk[4 * c + 3]);
-      }
+      for (int c = 0; c < 8; ++c)
+        st_shared_v4(p_row + ((c ^ (t & 7)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -345,107 +364,95 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(bars.ofull, (n_kv - 1) & 1, abort_flag, args.status, kStatusTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
     }
+    // combine the two halves of the row sum
+    float l_tot = l_run;
+    if (ok) {
+      rowsum[g * 128 + t] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars.xsum);
+      ok = mbar_wait(bars.xsum, 0, abort_flag, args.status, kStatusTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) l_tot = l_run + rowsum[(g ^ 1) * 128 + t];
+    }
     if (ok) {
       tc_fence_after();
       const int r = qblock * 128 + t;  // reordered row
       int pos = r < args.S ? (args.out_pos ? args.out_pos[r] : r) : -1;
       const bool in_seq = pos >= 0 && pos < args.S;  // a corrupt index writes nothing
-      const float inv_l = 1.f / l_run;
-      const float lse_h = (m_run + __log2f(l_run)) * 0.69314718055994531f;
-      const size_t bank_rows = static_cast<size_t>(bank) * args.S;
       if (!in_seq) pos = 0;
-      if (args.epilogue == 0) {
-        __nv_bfloat16* orow = args.o + (bank_rows + pos) * D;
+      const float inv_l = 1.f / l_tot;
+      const float lse_h = (m_run + __log2f(l_tot)) * 0.69314718055994531f;
+      const size_t bank_rows = static_cast<size_t>(bank) * args.S;
+      __nv_bfloat16* orow = args.o + (bank_rows + pos) * D;
+      const bool video = args.epilogue == 1 && r < args.rows;
+      float wh = 1.f, wt = 0.f, ms = 0.f, mc = 0.f, inv_td = 0.f, inv_den = 1.f;
+      size_t vrow = 0;
+      if (video) {
+        // corrected merge (recap/kernels/detail_cache.py:267-292)
+        vrow = static_cast<size_t>(bank) * args.rows + r;
+        const float gl = args.gl[vrow];
+        const float dl = args.dl[vrow];
+        const float ogl = args.ogl[vrow];
+        const float cshift = args.center[bank];
+        const float admit = expf(-fabsf(gl - ogl - cshift));
+        const float cl = gl + dl;
+        const float tc = fmaxf(gl, cl);
+        ms = (1.f - admit) * expf(gl - tc);
+        mc = admit * expf(cl - tc);
+        const float td = fmaxf(ms + mc, 1.0e-30f);
+        inv_td = 1.f / td;
+        const float tail_l = tc + logf(td);
+        const float common = fmaxf(lse_h, tail_l);
+        wh = expf(lse_h - common);
+        wt = expf(tail_l - common);
+        inv_den = 1.f / fmaxf(wh + wt, 1.0e-30f);
+      }
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          tmem_ld32(t_o + c * 32 + lane_base, v);
-          tmem_wait_ld();
-          if (in_seq) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w;
-              w.x = pack_bf16(v[8 * q + 0] * inv_l, v[8 * q + 1] * inv_l);
-              w.y = pack_bf16(v[8 * q + 2] * inv_l, v[8 * q + 3] * inv_l);
-              w.z = pack_bf16(v[8 * q + 4] * inv_l, v[8 * q + 5] * inv_l);
-              w.w = pack_bf16(v[8 * q + 6] * inv_l, v[8 * q + 7] * inv_l);
-              dst[q] = w;
-            }
-          }
-        }
-        if (in_seq && args.lse) args.lse[bank_rows + pos] = lse_h;
-      } else {
-        // corrected merge (recap/kernels/detail_cache.py:220-301)
-        const bool video = r < args.rows;
-        float wh = 1.f, wt = 0.f, ms = 0.f, mc = 0.f, inv_td = 0.f, inv_den = 1.f;
-        size_t vrow = 0;
+      for (int c = 0; c < D / 64; ++c) {
+        const int c0 = g * (D / 2) + c * 32;  // first output column of this chunk
+        float v[32];
+        tmem_ld32(t_o + c0 + lane_base, v);
+        tmem_wait_ld();
+        if (!in_seq) continue;
+        float res[32];
         if (video) {
-          vrow = static_cast<size_t>(bank) * args.rows + r;
-          const float gl = args.gl[vrow];
-          const float dl = args.dl[vrow];
-          const float ogl = args.ogl[vrow];
-          const float cshift = args.center[bank];
-          const float admit = expf(-fabsf(gl - ogl - cshift));
-          const float cl = gl + dl;
-          const float tc = fmaxf(gl, cl);
-          ms = (1.f - admit) * expf(gl - tc);
-          mc = admit * expf(cl - tc);
-          const float td = fmaxf(ms + mc, 1.0e-30f);
-          inv_td = 1.f / td;
-          const float tail_l = tc + logf(td);
-          const float common = fmaxf(lse_h, tail_l);
-          wh = expf(lse_h - common);
-          wt = expf(tail_l - common);
-          inv_den = 1.f / fmaxf(wh + wt, 1.0e-30f);
-        }
-        __nv_bfloat16* orow = args.o + (bank_rows + pos) * D;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          tmem_ld32(t_o + c * 32 + lane_base, v);
-          tmem_wait_ld();
-          if (!in_seq) continue;
-          float res[32];
-          if (video) {
-            const uint4* gsrc = reinterpret_cast<const uint4*>(args.go + vrow * D + c * 32);
-            const uint4* dsrc = reinterpret_cast<const uint4*>(args.det + vrow * D + c * 32);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 gw = gsrc[q];
-              const uint4 dw = dsrc[q];
-              const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw);
-              const __half2* d2 = reinterpret_cast<const __half2*>(&dw);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 gf = __bfloat1622float2(g2[e]);
-                const float2 df = __half22float2(d2[e]);
-                const int i0 = 8 * q + 2 * e;
-                const float oh0 = bf16_round(v[i0] * inv_l);
-                const float oh1 = bf16_round(v[i0 + 1] * inv_l);
-                const float to0 = (gf.x * ms + (gf.x + df.x) * mc) * inv_td;
-                const float to1 = (gf.y * ms + (gf.y + df.y) * mc) * inv_td;
-                res[i0] = (oh0 * wh + to0 * wt) * inv_den;
-                res[i0 + 1] = (oh1 * wh + to1 * wt) * inv_den;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) res[i] = v[i] * inv_l;
-          }
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+          const uint4* gsrc = reinterpret_cast<const uint4*>(args.go + vrow * D + c0);
+          const uint4* dsrc = reinterpret_cast<const uint4*>(args.det + vrow * D + c0);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = pack_bf16(res[8 * q + 0], res[8 * q + 1]);
-            w.y = pack_bf16(res[8 * q + 2], res[8 * q + 3]);
-            w.z = pack_bf16(res[8 * q + 4], res[8 * q + 5]);
-            w.w = pack_bf16(res[8 * q + 6], res[8 * q + 7]);
-            dst[q] = w;
+            const uint4 gw = gsrc[q];
+            const uint4 dw = dsrc[q];
+            const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw);
+            const __half2* d2 = reinterpret_cast<const __half2*>(&dw);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 gf = __bfloat1622float2(g2[e]);
+              const float2 df = __half22float2(d2[e]);
+              const int i0 = 8 * q + 2 * e;
+              const float oh0 = bf16_round(v[i0] * inv_l);
+              const float oh1 = bf16_round(v[i0 + 1] * inv_l);
+              const float to0 = (gf.x * ms + (gf.x + df.x) * mc) * inv_td;
+              const float to1 = (gf.y * ms + (gf.y + df.y) * mc) * inv_td;
+              res[i0] = (oh0 * wh + to0 * wt) * inv_den;
+              res[i0 + 1] = (oh1 * wh + to1 * wt) * inv_den;
+            }
           }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) res[i] = v[i] * inv_l;
         }
-        if (in_seq && args.lse) args.lse[bank_rows + pos] = lse_h;
+        uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16(res[8 * q + 0], res[8 * q + 1]);
+          w.y = pack_bf16(res[8 * q + 2], res[8 * q + 3]);
+          w.z = pack_bf16(res[8 * q + 4], res[8 * q + 5]);
+          w.w = pack_bf16(res[8 * q + 6], res[8 * q + 7]);
+          dst[q] = w;
+        }
       }
+      if (g == 0 && in_seq && args.lse) args.lse[bank_rows + pos] = lse_h;
     }
   }
   tc_fence_before();
