@@ -141,11 +141,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ================================================================ producer
     if (lane == 0) {
+      const uint64_t keep = l2_evict_last();    // per-bank operands: read by every query block
+      const uint64_t stream = l2_evict_first(); // the Q tile: read once here
       const int qrow = bank * a.S_pad + qb * 128;
       mbar_expect_tx(bars.pro_full, kTileQ + 2 * D * D * 2);
 #pragma unroll
       for (int at = 0; at < D / 64; ++at) {
-        tma_load_2d(sQ + at * 128 * 128, &tm_q, bars.pro_full, at * 64, qrow);
+        tma_load_2d_hint(sQ + at * 128 * 128, &tm_q, bars.pro_full, at * 64, qrow, stream);
         tma_load_2d(sRing + at * D * 128, &tm_ut, bars.pro_full, at * 64, bank * D);
         tma_load_2d(sRing + D * D * 2 + at * D * 128, &tm_c, bars.pro_full, at * 64, bank * D);
       }
@@ -162,10 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(bars.full + st, L::kStage);
 #pragma unroll
         for (int at = 0; at < D / 64; ++at) {
-          tma_load_2d(base + at * kTileN * 128, &tm_kbar, bars.full + st, at * 64, brow);
-          tma_load_2d(base + L::kOpK + at * kTileN * 128, &tm_w, bars.full + st, at * 64, brow);
+          tma_load_2d_hint(base + at * kTileN * 128, &tm_kbar, bars.full + st, at * 64, brow, keep);
+          tma_load_2d_hint(base + L::kOpK + at * kTileN * 128, &tm_w, bars.full + st, at * 64, brow, keep);
         }
-        tma_load_2d(base + L::kOpK + L::kOpW, &tm_vbt, bars.full + st, j * kTileN, bank * D);
+        tma_load_2d_hint(base + L::kOpK + L::kOpW, &tm_vbt, bars.full + st, j * kTileN, bank * D, keep);
       }
       const int first = j > kStages ? j - kStages : 0;
       for (int k = first; k < j; ++k) mbar_drain(bars.full + (k % kStages), (k / kStages) & 1);
@@ -397,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) d4[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        for (int q = 0; q < 4; ++q) st_stream_v4(d4 + q, make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]));
       }
       a.lse[orow] = lse;
       if (a.center_partial != nullptr) {

@@ -161,10 +161,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_vt);
+      const uint64_t keep = l2_evict_last();    // K and V tiles: re-read by many CTAs
+      const uint64_t stream = l2_evict_first(); // the Q tile: read once
       const int qrow = bank * args.S_pad + qblock * 128;
       mbar_expect_tx(bars.qfull, kTileBytes);
 #pragma unroll
-      for (int a = 0; a < D / 64; ++a) tma_load_2d(sQ + a * 128 * 128, &tm_q, bars.qfull, a * 64, qrow);
+      for (int a = 0; a < D / 64; ++a)
+        tma_load_2d_hint(sQ + a * 128 * 128, &tm_q, bars.qfull, a * 64, qrow, stream);
       const int n_items = 2 * n_kv;
       int i = 0;
       for (; i < n_items; ++i) {
@@ -181,11 +184,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int krow = bank * args.S_pad + blk * 128;
 #pragma unroll
           for (int a = 0; a < D / 64; ++a)
-            tma_load_2d(dst + a * 128 * 128, &tm_k, bars.full + slot, a * 64, krow);
+            tma_load_2d_hint(dst + a * 128 * 128, &tm_k, bars.full + slot, a * 64, krow, keep);
         } else {
 #pragma unroll
           for (int a = 0; a < 2; ++a)
-            tma_load_2d(dst + a * D * 128, &tm_vt, bars.full + slot, blk * 128 + a * 64, bank * D);
+            tma_load_2d_hint(dst + a * D * 128, &tm_vt, bars.full + slot, blk * 128 + a * 64, bank * D, keep);
         }
       }
       // Leave no bulk copy in flight: wait for the last loads this thread issued.
@@ -420,8 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint4* dsrc = reinterpret_cast<const uint4*>(args.det + vrow * D + c0);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const uint4 gw = gsrc[q];
-            const uint4 dw = dsrc[q];
+            const uint4 gw = ld_stream_v4(gsrc + q);
+            const uint4 dw = ld_stream_v4(dsrc + q);
             const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw);
             const __half2* d2 = reinterpret_cast<const __half2*>(&dw);
 #pragma unroll
@@ -449,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           w.y = pack_bf16(res[8 * q + 2], res[8 * q + 3]);
           w.z = pack_bf16(res[8 * q + 4], res[8 * q + 5]);
           w.w = pack_bf16(res[8 * q + 6], res[8 * q + 7]);
-          dst[q] = w;
+          st_stream_v4(dst + q, w);
         }
       }
       if (g == 0 && in_seq && args.lse) args.lse[bank_rows + pos] = lse_h;
