@@ -4,22 +4,32 @@
 // call of recap/kernels/block_sparse.py:78-139 and the dense flash call of
 // recap/operator.py:254-256 (the same kernel run with every key block kept).
 //
-// One CTA per (bank, query block); 12 warps:
-//   warp 0      TMA producer: the Q tile once, then K and V^T tiles of every kept
-//               key block through a ring of NST shared-memory slots;
-//   warp 1      TMEM allocator and MMA issuer (one thread): S = Q K^T into one of
-//               two TMEM S buffers, O += P V into the TMEM O accumulator;
-//   warps 4-11  softmax, two warpgroups per query tile: each query row is shared by
-//               one thread of each group (TMEM lane = row), group g taking key columns
-//               [64g, 64g + 64) of S and output columns [D/2 g, D/2 (g+1)).  The groups
-//               exchange row maxima each tile, so both rescale with the same running
-//               max (log2 domain, lazy rescaling of O), write their half of P as bf16 to
-//               shared memory, and split the epilogue.  Two softmax warps per SM
-//               sub-partition hide each other's latency.
+// One CTA per (bank, pair of query blocks A and B); 10 warps:
+//   warp 0      TMA producer: both Q tiles, then the K and V^T tiles in the order the
+//               MMA warp consumes them, through a ring of NST shared-memory slots;
+//   warp 1      TMEM allocator and MMA issuer (one thread);
+//   warps 2-5   softmax and epilogue of tile A, warps 6-9 of tile B: one query row per
+//               thread (TMEM lane = row), online softmax in the log2 domain with lazy
+//               rescaling of O.
+// Key-block order: each tile's kept list is reordered so that the blocks both tiles
+// keep come first, in the same order.  For those rounds one K tile and one V^T tile in
+// shared memory serve both tiles; afterwards each tile streams its own blocks.  The
+// softmax order of blocks does not change the result beyond fp32 rounding.
+//
+// TMEM (512 columns): S_A [0,128), S_B [128,256), O_A [256,256+D), O_B [256+D,256+2D).
+// P_x (bf16, two per column) overwrites the first 64 columns of S_x and is the A
+// operand of O_x += P_x V straight from TMEM.  MMA issue order:
+//   S_A(0) S_B(0), then for r = 0, 1, ...:  PV_A(r) S_A(r+1) PV_B(r) S_B(r+1)
+// so the tensor core computes one tile's products while the other tile's softmax
+// runs.  S_x(r+1) is issued after PV_x(r) by the same thread, so it overwrites P_x(r)
+// only after that product has read it (tcgen05.mma operations of one thread execute
+// in issue order), and the commit that signals S_x(r+1) also covers PV_x(r): when the
+// softmax sees S_x(r+1), O_x is complete up to block r and may be rescaled.
+//
 // The epilogue either writes O (bf16) and LSE, or applies the corrected merge of
-// recap/kernels/detail_cache.py:188-301 (drift-weighted refinement + coarse
-// tail, merged in log-mass space) and writes the result straight to the native
-// token order (the Layout.restore gather of recap/sparse/layout.py:90-92).
+// recap/kernels/detail_cache.py:188-301 (drift-weighted refinement + coarse tail,
+// merged in log-mass space) and writes the result straight to the native token
+// order (the Layout.restore gather of recap/sparse/layout.py:90-92).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -27,39 +37,28 @@ namespace recap {
 
 namespace {
 
-constexpr int kThreads = 384;
-constexpr int kSoftmaxWarp0 = 4;
+constexpr int kThreads = 320;
+constexpr int kSoftmaxWarp0 = 2;
 constexpr int kMaxKeyBlocks = 2048;
-constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when max grows by 2^8
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by 2^8
 
 template <int D>
 struct FmhaSmem {
   static constexpr int kTileBytes = 128 * D * 2;  // Q, K (128 x D) and V^T (D x 128) tiles
-  static constexpr int kNst = 4;
-  static constexpr int kQ = 0;
-  static constexpr int kP = kQ + kTileBytes;
-  static constexpr int kKV = kP + 128 * 128 * 2;
+  static constexpr int kNst = D == 128 ? 4 : 8;
+  static constexpr int kQ = 0;                        // Q_A, Q_B
+  static constexpr int kKV = kQ + 2 * kTileBytes;     // ring of K / V^T tiles
   static constexpr int kBars = kKV + kNst * kTileBytes;
-  // barriers: qfull, full[NST], empty[NST], sfull[2], sfree[2], pfull, ofull, done, xchg[2], xsum
-  static constexpr int kNumBars = 1 + 2 * kNst + 2 + 2 + 3 + 3;
-  static constexpr int kMisc = kBars + kNumBars * 8;  // tmem addr, abort flag, list length
-  static constexpr int kList = kMisc + 16;
-  static constexpr int kRowMax = kList + kMaxKeyBlocks * 4;  // [2 parity][2 halves][128] fp32
-  static constexpr int kRowSum = kRowMax + 2 * 2 * 128 * 4;  // [2 halves][128] fp32
-  static constexpr int kTotal = kRowSum + 2 * 128 * 4;
+  // qfull, full[NST], empty[NST], sfull[2], pfull[2], ofin[2], done
+  static constexpr int kNumBars = 1 + 2 * kNst + 7;
+  static constexpr int kMisc = kBars + kNumBars * 8;  // tmem base, abort flag, LA, LB, nS
+  static constexpr int kList = kMisc + 32;            // uint16 list_a[2048], only_b[2048]
+  static constexpr int kRows = kList + 2 * kMaxKeyBlocks * 2;  // staged partition rows, 2 x 2048 bytes
+  static constexpr int kTotal = kRows + 2 * kMaxKeyBlocks;
 };
 
 struct Bars {
-  uint64_t* qfull;
-  uint64_t* full;
-  uint64_t* empty;
-  uint64_t* sfull;
-  uint64_t* sfree;
-  uint64_t* pfull;
-  uint64_t* ofull;
-  uint64_t* done;
-  uint64_t* xchg;  // [2] row-max exchange between the two softmax warpgroups, by tile parity
-  uint64_t* xsum;  // row-sum exchange at the end
+  uint64_t *qfull, *full, *empty, *sfull, *pfull, *ofin, *done;
 };
 
 template <int NST>
@@ -70,13 +69,75 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* base) {
   r.full = b + 1;
   r.empty = b + 1 + NST;
   r.sfull = b + 1 + 2 * NST;
-  r.sfree = b + 3 + 2 * NST;
-  r.pfull = b + 5 + 2 * NST;
-  r.ofull = b + 6 + 2 * NST;
+  r.pfull = b + 3 + 2 * NST;
+  r.ofin = b + 5 + 2 * NST;
   r.done = b + 7 + 2 * NST;
-  r.xchg = b + 8 + 2 * NST;
-  r.xsum = b + 10 + 2 * NST;
   return r;
+}
+
+// The two query blocks of this CTA.  Dense query blocks (attending every key block)
+// come first over all banks, then the sparse ones; pairs are adjacent blocks of the
+// reordered sequence.  qb < 0: the CTA has one tile.
+struct Item {
+  int bank, qa, qb;
+};
+
+__device__ __forceinline__ Item decode_item(const FmhaArgs& a) {
+  Item it;
+  const int NB = a.NB;
+  int b = blockIdx.x;
+  if (a.all_blocks) {
+    const int per = (NB + 1) / 2;
+    it.bank = b / per;
+    const int k = b - it.bank * per;
+    it.qa = 2 * k;
+    it.qb = 2 * k + 1 < NB ? 2 * k + 1 : -1;
+    return it;
+  }
+  const int nd_items = (NB - a.dense_start + 1) / 2;
+  const int ns_items = (a.dense_start + 1) / 2;
+  if (b < a.banks * nd_items) {
+    it.bank = b / nd_items;
+    const int k = b - it.bank * nd_items;
+    it.qa = a.dense_start + 2 * k;
+    it.qb = it.qa + 1 < NB ? it.qa + 1 : -1;
+  } else {
+    b -= a.banks * nd_items;
+    it.bank = b / ns_items;
+    const int k = b - it.bank * ns_items;
+    it.qa = 2 * k;
+    it.qb = 2 * k + 1 < a.dense_start ? 2 * k + 1 : -1;
+  }
+  return it;
+}
+
+__host__ __device__ __forceinline__ int fmha_grid(int banks, int NB, int dense_start, int all_blocks) {
+  if (all_blocks) return banks * ((NB + 1) / 2);
+  return banks * ((NB - dense_start + 1) / 2 + (dense_start + 1) / 2);
+}
+
+enum : int { kOpS = 0, kOpPV = 1 };
+
+// The MMA op sequence shared by the producer and the MMA issuer:
+//   S_A(0) S_B(0), then per round r: PV_A(r) S_A(r+1) PV_B(r) S_B(r+1)
+// with the ops of an exhausted tile dropped.  `op(tile, kind, round)` returns false to
+// stop the walk.
+template <typename Op>
+__device__ __forceinline__ bool walk_ops(int LA, int LB, Op&& op) {
+  if (LA > 0 && !op(0, kOpS, 0)) return false;
+  if (LB > 0 && !op(1, kOpS, 0)) return false;
+  const int R = LA > LB ? LA : LB;
+  for (int r = 0; r < R; ++r) {
+    if (r < LA) {
+      if (!op(0, kOpPV, r)) return false;
+      if (r + 1 < LA && !op(0, kOpS, r + 1)) return false;
+    }
+    if (r < LB) {
+      if (!op(1, kOpPV, r)) return false;
+      if (r + 1 < LB && !op(1, kOpS, r + 1)) return false;
+    }
+  }
+  return true;
 }
 
 template <int D>
@@ -91,291 +152,293 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem + L::kQ;
-  uint8_t* sP = smem + L::kP;
   uint8_t* sKV = smem + L::kKV;
   Bars bars = carve_bars<NST>(smem + L::kBars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
-  int* list_len = reinterpret_cast<int*>(smem + L::kMisc + 8);
-  int* list = reinterpret_cast<int*>(smem + L::kList);
-  float* rowmax = reinterpret_cast<float*>(smem + L::kRowMax);
-  float* rowsum = reinterpret_cast<float*>(smem + L::kRowSum);
+  int* lens = reinterpret_cast<int*>(smem + L::kMisc + 8);  // LA, LB, nS
+  uint16_t* list_a = reinterpret_cast<uint16_t*>(smem + L::kList);
+  uint16_t* only_b = list_a + kMaxKeyBlocks;
+  uint8_t* row_a = smem + L::kRows;
+  uint8_t* row_b = row_a + kMaxKeyBlocks;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // ---- work item: bank-major; within a bank the long dense query blocks first
+  const Item it = decode_item(args);
   const int NB = args.NB;
-  const int bank = blockIdx.x / NB;
-  const int item = blockIdx.x - bank * NB;
-  const int n_dense_rows = NB - args.dense_start;
-  int qblock = item < n_dense_rows ? args.dense_start + item : item - n_dense_rows;
-  if (args.all_blocks) qblock = item;
-  const bool dense_row = args.all_blocks || qblock >= args.dense_start;
+  const bool has_b = it.qb >= 0;
+  const bool dense_a = args.all_blocks || it.qa >= args.dense_start;
+  const bool dense_b = args.all_blocks || (has_b && it.qb >= args.dense_start);
 
-  // ---- setup: barriers, TMEM, key-block list
+  // ---- setup: barriers and TMEM
   if (threadIdx.x == 0) {
     mbar_init(bars.qfull, 1);
     for (int s = 0; s < NST; ++s) {
       mbar_init(bars.full + s, 1);
       mbar_init(bars.empty + s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bars.sfull + b, 1);
-      mbar_init(bars.sfree + b, 8);  // both softmax warpgroups read each S buffer
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bars.sfull + x, 1);
+      mbar_init(bars.pfull + x, 4);  // one arrival per softmax warp of the tile
+      mbar_init(bars.ofin + x, 1);
     }
-    mbar_init(bars.pfull, 8);
-    mbar_init(bars.ofull, 1);
     mbar_init(bars.done, 1);
-    mbar_init(bars.xchg, 8);
-    mbar_init(bars.xchg + 1, 8);
-    mbar_init(bars.xsum, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
-  if (warp == 0) {
-    int count = 0;
-    const uint8_t* prow =
-        args.partition + (static_cast<size_t>(bank) * args.nB + (dense_row ? 0 : qblock)) * args.nB;
-    for (int base = 0; base < NB; base += 32) {
-      const int j = base + lane;
-      bool keep = false;
-      if (j < NB) keep = dense_row || j >= args.dense_start || prow[j] != 0;
-      const unsigned m = __ballot_sync(0xffffffffu, keep);
-      if (keep) list[count + __popc(m & ((1u << lane) - 1u))] = j;
-      count += __popc(m);
-    }
-    if (lane == 0) *list_len = count;
-  }
   __syncthreads();
   tc_fence_after();
+
+  // ---- the Q tiles do not depend on the key lists: load them first
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_vt);
+    const uint64_t stream = l2_evict_first();  // query tiles are read once
+    mbar_expect_tx(bars.qfull, has_b ? 2 * kTileBytes : kTileBytes);
+    const int qrow_a = it.bank * args.S_pad + it.qa * 128;
+#pragma unroll
+    for (int a = 0; a < D / 64; ++a) tma_load_2d_hint(sQ + a * 128 * 128, &tm_q, bars.qfull, a * 64, qrow_a, stream);
+    if (has_b) {
+      const int qrow_b = it.bank * args.S_pad + it.qb * 128;
+#pragma unroll
+      for (int a = 0; a < D / 64; ++a)
+        tma_load_2d_hint(sQ + kTileBytes + a * 128 * 128, &tm_q, bars.qfull, a * 64, qrow_b, stream);
+    }
+  }
+
+  // ---- key-block lists: stage the two partition rows (independent loads), then
+  // one warp splits them into blocks kept by both / by A only / by B only.
+  const size_t part_bank = static_cast<size_t>(it.bank) * args.nB;
+  if (!dense_a) {
+    const uint8_t* p = args.partition + (part_bank + it.qa) * args.nB;
+    for (int j = threadIdx.x; j < args.dense_start; j += kThreads) row_a[j] = p[j];
+  }
+  if (has_b && !dense_b) {
+    const uint8_t* p = args.partition + (part_bank + it.qb) * args.nB;
+    for (int j = threadIdx.x; j < args.dense_start; j += kThreads) row_b[j] = p[j];
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned below = (1u << lane) - 1u;
+    auto kept = [&](int j, bool& ka, bool& kb) {
+      const bool in = j < NB;
+      const bool forced = j >= args.dense_start;
+      ka = in && (dense_a || forced || row_a[j] != 0);
+      kb = in && has_b && (dense_b || forced || row_b[j] != 0);
+    };
+    int n_shared = 0;
+    for (int base = 0; base < NB; base += 32) {
+      bool ka, kb;
+      kept(base + lane, ka, kb);
+      n_shared += __popc(__ballot_sync(0xffffffffu, ka && kb));
+    }
+    int cs = 0, ca = 0, cb = 0;
+    for (int base = 0; base < NB; base += 32) {
+      const int j = base + lane;
+      bool ka, kb;
+      kept(j, ka, kb);
+      const unsigned ms = __ballot_sync(0xffffffffu, ka && kb);
+      const unsigned ma = __ballot_sync(0xffffffffu, ka && !kb);
+      const unsigned mb = __ballot_sync(0xffffffffu, kb && !ka);
+      if (ka && kb) list_a[cs + __popc(ms & below)] = static_cast<uint16_t>(j);
+      if (ka && !kb) list_a[n_shared + ca + __popc(ma & below)] = static_cast<uint16_t>(j);
+      if (kb && !ka) only_b[cb + __popc(mb & below)] = static_cast<uint16_t>(j);
+      cs += __popc(ms);
+      ca += __popc(ma);
+      cb += __popc(mb);
+    }
+    if (lane == 0) {
+      lens[0] = n_shared + ca;
+      lens[1] = has_b ? n_shared + cb : 0;
+      lens[2] = n_shared;
+    }
+  }
+  __syncthreads();
   const uint32_t tmem = *tmem_slot;
-  const int n_kv = *list_len;
-  const uint32_t t_s = tmem;           // S buffers: columns [0,128) and [128,256)
-  const uint32_t t_o = tmem + 256;     // O accumulator: columns [256, 256 + D)
+  const int LA = lens[0];
+  const int LB = lens[1];
+  const int nS = lens[2];
+  auto block_of = [&](int x, int round) -> int {
+    return (x == 0 || round < nS) ? list_a[round] : only_b[round - nS];
+  };
 
   if (warp == 0) {
     // ================================================================ producer
-    if (lane == 0 && n_kv > 0) {
-      prefetch_tmap(&tm_q);
-      prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_vt);
-      const uint64_t keep = l2_evict_last();    // K and V tiles: re-read by many CTAs
-      const uint64_t stream = l2_evict_first(); // the Q tile: read once
-      const int qrow = bank * args.S_pad + qblock * 128;
-      mbar_expect_tx(bars.qfull, kTileBytes);
-#pragma unroll
-      for (int a = 0; a < D / 64; ++a)
-        tma_load_2d_hint(sQ + a * 128 * 128, &tm_q, bars.qfull, a * 64, qrow, stream);
-      const int n_items = 2 * n_kv;
-      int i = 0;
-      for (; i < n_items; ++i) {
-        const int slot = i % NST;
-        if (i >= NST) {
-          if (!mbar_wait(bars.empty + slot, ((i / NST) - 1) & 1, abort_flag, args.status,
-                         kStatusTimeoutProducer))
-            break;
-        }
+    if (lane == 0 && LA + LB > 0) {
+      const uint64_t keep = l2_evict_last();  // K and V tiles: re-read by many CTAs
+      int load_no = 0;
+      walk_ops(LA, LB, [&](int x, int kind, int round) -> bool {
+        if (x == 1 && round < nS) return true;  // the tile-A op of this round loaded it
+        const int slot = load_no % NST;
+        if (load_no >= NST &&
+            !mbar_wait(bars.empty + slot, ((load_no / NST) - 1) & 1, abort_flag, args.status,
+                       kStatusTimeoutProducer))
+          return false;
         uint8_t* dst = sKV + slot * kTileBytes;
-        const int blk = list[i >> 1];
+        const int blk = block_of(x, round);
         mbar_expect_tx(bars.full + slot, kTileBytes);
-        if ((i & 1) == 0) {
-          const int krow = bank * args.S_pad + blk * 128;
+        if (kind == kOpS) {
+          const int krow = it.bank * args.S_pad + blk * 128;
 #pragma unroll
           for (int a = 0; a < D / 64; ++a)
             tma_load_2d_hint(dst + a * 128 * 128, &tm_k, bars.full + slot, a * 64, krow, keep);
         } else {
 #pragma unroll
           for (int a = 0; a < 2; ++a)
-            tma_load_2d_hint(dst + a * D * 128, &tm_vt, bars.full + slot, blk * 128 + a * 64, bank * D, keep);
+            tma_load_2d_hint(dst + a * D * 128, &tm_vt, bars.full + slot, blk * 128 + a * 64, it.bank * D, keep);
         }
-      }
+        ++load_no;
+        return true;
+      });
       // Leave no bulk copy in flight: wait for the last loads this thread issued.
-      const int first = i > NST ? i - NST : 0;
-      for (int k = first; k < i; ++k) {
-        const int slot = k % NST;
-        mbar_drain(bars.full + slot, (k / NST) & 1);
-      }
-      mbar_drain(bars.qfull, 0);
+      const int first = load_no > NST ? load_no - NST : 0;
+      for (int k = first; k < load_no; ++k) mbar_drain(bars.full + (k % NST), (k / NST) & 1);
     }
+    if (lane == 0) mbar_drain(bars.qfull, 0);
   } else if (warp == 1) {
     // ================================================================ MMA issuer
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0 && LA + LB > 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, D);
       const uint32_t q_base = smem_u32(sQ);
-      const uint32_t p_base = smem_u32(sP);
       const uint32_t kv_base = smem_u32(sKV);
-      bool ok = mbar_wait(bars.qfull, 0, abort_flag, args.status, kStatusTimeoutTma);
-      auto issue_s = [&](int j) -> bool {
-        const int item_k = 2 * j;
-        const int slot = item_k % NST;
-        if (!mbar_wait(bars.full + slot, (item_k / NST) & 1, abort_flag, args.status,
-                       kStatusTimeoutTma))
-          return false;
-        const int b = j & 1;
-        if (j >= 2 && !mbar_wait(bars.sfree + b, ((j >> 1) - 1) & 1, abort_flag, args.status,
-                                 kStatusTimeoutMma))
-          return false;
-        tc_fence_after();
-        const uint32_t k_base = kv_base + slot * kTileBytes;
+      int load_no = 0;
+      int slot_k = 0, slot_v = 0;  // latest slot of each kind (K for S, V^T for PV)
+      if (mbar_wait(bars.qfull, 0, abort_flag, args.status, kStatusTimeoutTma)) {
+        walk_ops(LA, LB, [&](int x, int kind, int round) -> bool {
+          const bool reuse = x == 1 && round < nS;
+          int slot;
+          if (!reuse) {
+            slot = load_no % NST;
+            if (!mbar_wait(bars.full + slot, (load_no / NST) & 1, abort_flag, args.status, kStatusTimeoutTma))
+              return false;
+            ++load_no;
+            if (kind == kOpS)
+              slot_k = slot;
+            else
+              slot_v = slot;
+          } else {
+            slot = kind == kOpS ? slot_k : slot_v;
+          }
+          const uint32_t t_sx = tmem + 128 * x;
+          const uint32_t tile = kv_base + slot * kTileBytes;
+          if (kind == kOpS) {
+            tc_fence_after();
+            const uint32_t qx = q_base + x * kTileBytes;
 #pragma unroll
-        for (int s = 0; s < D / 16; ++s) {
-          const uint32_t off = (s >> 2) * (128 * 128) + (s & 3) * 32;
-          mma_bf16_ss(t_s + b * 128, sdesc_k_sw128(q_base + off), sdesc_k_sw128(k_base + off),
-                      idesc_s, s > 0);
-        }
-        mma_commit(bars.sfull + b);
-        mma_commit(bars.empty + slot);
-        return true;
-      };
-      auto issue_pv = [&](int j) -> bool {
-        if (!mbar_wait(bars.pfull, j & 1, abort_flag, args.status, kStatusTimeoutMma)) return false;
-        const int item_v = 2 * j + 1;
-        const int slot = item_v % NST;
-        if (!mbar_wait(bars.full + slot, (item_v / NST) & 1, abort_flag, args.status,
-                       kStatusTimeoutTma))
-          return false;
-        tc_fence_after();
-        const uint32_t v_base = kv_base + slot * kTileBytes;
+            for (int s = 0; s < D / 16; ++s) {
+              const uint32_t off = (s >> 2) * (128 * 128) + (s & 3) * 32;
+              mma_bf16_ss(t_sx, sdesc_k_sw128(qx + off), sdesc_k_sw128(tile + off), idesc_s, s > 0);
+            }
+            mma_commit(bars.sfull + x);
+          } else {
+            if (!mbar_wait(bars.pfull + x, round & 1, abort_flag, args.status, kStatusTimeoutMma)) return false;
+            tc_fence_after();
+            const uint32_t t_ox = tmem + 256 + D * x;
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          const uint32_t off_p = (s >> 2) * (128 * 128) + (s & 3) * 32;
-          const uint32_t off_v = (s >> 2) * (D * 128) + (s & 3) * 32;
-          mma_bf16_ss(t_o, sdesc_k_sw128(p_base + off_p), sdesc_k_sw128(v_base + off_v), idesc_o,
-                      (j > 0 || s > 0) ? 1u : 0u);
-        }
-        mma_commit(bars.empty + slot);
-        mma_commit(bars.ofull);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 1; ok && j < n_kv; ++j) {
-        ok = issue_s(j);
-        if (ok) ok = issue_pv(j - 1);
+            for (int s = 0; s < 8; ++s) {
+              const uint32_t off_v = (s >> 2) * (D * 128) + (s & 3) * 32;
+              mma_bf16_ts(t_ox, t_sx + 8 * s, sdesc_k_sw128(tile + off_v), idesc_o, (round > 0 || s > 0) ? 1u : 0u);
+            }
+            if (round == (x == 0 ? LA : LB) - 1) mma_commit(bars.ofin + x);
+          }
+          if (x == 1 || round >= nS) mma_commit(bars.empty + slot);  // last user of the slot
+          return true;
+        });
       }
-      if (ok) ok = issue_pv(n_kv - 1);
       // All MMAs issued by this thread complete before TMEM is released.
       mma_commit(bars.done);
       mbar_drain(bars.done, 0);
     }
-  } else if (warp >= kSoftmaxWarp0) {
+  } else {
     // ================================================================ softmax + epilogue
-    // Two warpgroups share every query row: group g handles key columns [64g, 64g + 64)
-    // of S and output columns [D/2 g, D/2 (g + 1)); the row max is exchanged through
-    // shared memory each tile so both groups use the same running max.
-    const int g = (warp - kSoftmaxWarp0) >> 2;   // column half
-    const int q4 = (warp - kSoftmaxWarp0) & 3;   // TMEM lane quarter
-    const int t = q4 * 32 + lane;                // query row within the block
+    const int x = (warp - kSoftmaxWarp0) >> 2;  // tile
+    const int q4 = warp & 3;                    // TMEM lane quarter this warp may access
+    const int t = q4 * 32 + lane;               // query row within the block
     const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
+    const int Lx = x == 0 ? LA : LB;
+    const int qblock = x == 0 ? it.qa : it.qb;
+    const uint32_t t_sx = tmem + 128 * x + lane_base;
+    const uint32_t t_ox = tmem + 256 + D * x + lane_base;
     const float scale_log2 = args.scale_log2;
-    float m_run = -INFINITY;  // running max, log2 domain (scaled), identical in both groups
-    float l_run = 0.f;        // this group's share of the row sum
-    const uint32_t p_row = smem_u32(sP) + g * 16384 + t * 128;  // P columns [64g, 64g + 64)
-    bool ok = n_kv > 0;
-    for (int j = 0; ok && j < n_kv; ++j) {
-      const int b = j & 1;
-      ok = mbar_wait(bars.sfull + b, (j >> 1) & 1, abort_flag, args.status, kStatusTimeoutSoftmax);
+    float m_run = -INFINITY;  // running max, log2 domain (scaled)
+    float l_run = 0.f;        // running row sum at m_run
+    bool ok = Lx > 0;
+    for (int r = 0; ok && r < Lx; ++r) {
+      ok = mbar_wait(bars.sfull + x, r & 1, abort_flag, args.status, kStatusTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      float x[64];
+      float s[128];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float v[32];
-        tmem_ld32(t_s + b * 128 + g * 64 + c * 32 + lane_base, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i];
-      }
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_sx + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bars.sfree + b);
       // keys past the end of the sequence (last, partial key block)
-      const int valid = args.S - list[j] * 128 - g * 64;
-      if (valid < 64) {
+      const int valid = args.S - block_of(x, r) * 128;
+      if (valid < 128) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (i >= valid) x[i] = -INFINITY;
+        for (int i = 0; i < 128; ++i)
+          if (i >= valid) s[i] = -INFINITY;
       }
-      float mxa[8];
+      float mx[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mxa[k] = x[k];
+      for (int k = 0; k < 8; ++k) mx[k] = max3(s[k], s[8 + k], s[16 + k]);
 #pragma unroll
-      for (int i = 8; i < 64; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], x[i]);
-      float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                       fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-      // exchange the half-row maxima (double-buffered by tile parity); an mbarrier with a
-      // bounded wait, so that a warpgroup that aborts cannot strand the other one
-      rowmax[(b * 2 + g) * 128 + t] = mx;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bars.xchg + b);
-      ok = mbar_wait(bars.xchg + b, (j >> 1) & 1, abort_flag, args.status, kStatusTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      mx = fmaxf(mx, rowmax[(b * 2 + (g ^ 1)) * 128 + t]);
-      const float m_tile = mx * scale_log2;
+      for (int i = 24; i < 128; i += 16) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], s[i + k], s[i + 8 + k]);
+      }
+      const float m_all = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+      const float m_tile = m_all * scale_log2;
       float alpha = 1.f;
       bool rescale = false;
-      if (j == 0) {
+      if (r == 0) {
         m_run = m_tile;
       } else if (m_tile > m_run + kRescaleThreshold) {
         alpha = fast_exp2(m_run - m_tile);
         m_run = m_tile;
         rescale = true;
       }
-      float sa[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[32];
+      const float neg_m = -m_run;
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = fast_exp2(fmaf(x[2 * i], scale_log2, -m_run));
-        const float p1 = fast_exp2(fmaf(x[2 * i + 1], scale_log2, -m_run));
-        sa[i & 3] += p0 + p1;
-        pk[i] = pack_bf16(p0, p1);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float y0, y1;
+          fma2(y0, y1, s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1], scale_log2, scale_log2, neg_m, neg_m);
+          const float p0 = fast_exp2(y0);
+          const float p1 = fast_exp2(y1);
+          add2(sum[(i & 1) * 2], sum[(i & 1) * 2 + 1], p0, p1);
+          pk[i] = pack_bf16(p0, p1);
+        }
+        tmem_st16(t_sx + c * 16, pk);
       }
-      l_run = l_run * alpha + ((sa[0] + sa[1]) + (sa[2] + sa[3]));
-      // PV(j-1) must be complete before P is overwritten and O is rescaled.
-      if (j > 0) {
-        ok = mbar_wait(bars.ofull, (j - 1) & 1, abort_flag, args.status, kStatusTimeoutSoftmax);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
+      // O holds P.V of blocks 0..r-1 complete (the commit of S(r) covers PV(r-1));
+      // PV(r) is not issued before this warp's pfull arrival below.
+      if (r > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 64; ++c) {
-            float v[32];
-            const uint32_t col = t_o + g * (D / 2) + c * 32 + lane_base;
-            tmem_ld32(col, v);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(t_ox + c * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= alpha;
-            tmem_st32(col, v);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; i += 2) mul2(o[i], o[i + 1], alpha, alpha);
+          tmem_st32(t_ox + c * 32, o);
         }
       }
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        st_shared_v4(p_row + ((c ^ (t & 7)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bars.pfull);
+      if (lane == 0) mbar_arrive(bars.pfull + x);
+      l_run = l_run * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
     }
     if (ok) {
-      ok = mbar_wait(bars.ofull, (n_kv - 1) & 1, abort_flag, args.status, kStatusTimeoutSoftmax);
+      ok = mbar_wait(bars.ofin + x, 0, abort_flag, args.status, kStatusTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
-    }
-    // combine the two halves of the row sum
-    float l_tot = l_run;
-    if (ok) {
-      rowsum[g * 128 + t] = l_run;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bars.xsum);
-      ok = mbar_wait(bars.xsum, 0, abort_flag, args.status, kStatusTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) l_tot = l_run + rowsum[(g ^ 1) * 128 + t];
     }
     if (ok) {
       tc_fence_after();
@@ -383,20 +446,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pos = r < args.S ? (args.out_pos ? args.out_pos[r] : r) : -1;
       const bool in_seq = pos >= 0 && pos < args.S;  // a corrupt index writes nothing
       if (!in_seq) pos = 0;
-      const float inv_l = 1.f / l_tot;
-      const float lse_h = (m_run + __log2f(l_tot)) * 0.69314718055994531f;
-      const size_t bank_rows = static_cast<size_t>(bank) * args.S;
+      const float inv_l = 1.f / l_run;
+      const float lse_h = (m_run + __log2f(l_run)) * 0.69314718055994531f;
+      const size_t bank_rows = static_cast<size_t>(it.bank) * args.S;
       __nv_bfloat16* orow = args.o + (bank_rows + pos) * D;
       const bool video = args.epilogue == 1 && r < args.rows;
       float wh = 1.f, wt = 0.f, ms = 0.f, mc = 0.f, inv_td = 0.f, inv_den = 1.f;
       size_t vrow = 0;
       if (video) {
         // corrected merge (recap/kernels/detail_cache.py:267-292)
-        vrow = static_cast<size_t>(bank) * args.rows + r;
+        vrow = static_cast<size_t>(it.bank) * args.rows + r;
         const float gl = args.gl[vrow];
         const float dl = args.dl[vrow];
         const float ogl = args.ogl[vrow];
-        const float cshift = args.center[bank];
+        const float cshift = args.center[it.bank];
         const float admit = expf(-fabsf(gl - ogl - cshift));
         const float cl = gl + dl;
         const float tc = fmaxf(gl, cl);
@@ -411,10 +474,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         inv_den = 1.f / fmaxf(wh + wt, 1.0e-30f);
       }
 #pragma unroll 1
-      for (int c = 0; c < D / 64; ++c) {
-        const int c0 = g * (D / 2) + c * 32;  // first output column of this chunk
+      for (int c = 0; c < D / 32; ++c) {
+        const int c0 = c * 32;  // first output column of this chunk
         float v[32];
-        tmem_ld32(t_o + c0 + lane_base, v);
+        tmem_ld32(t_ox + c0, v);
         tmem_wait_ld();
         if (!in_seq) continue;
         float res[32];
@@ -455,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           st_stream_v4(dst + q, w);
         }
       }
-      if (g == 0 && in_seq && args.lse) args.lse[bank_rows + pos] = lse_h;
+      if (in_seq && args.lse) args.lse[bank_rows + pos] = lse_h;
     }
   }
   tc_fence_before();
@@ -469,19 +532,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 int launch_fmha(const FmhaLaunch& L, cudaStream_t stream) {
-  if (L.args.NB > kMaxKeyBlocks) return kErrShape;
-  const int grid = L.args.banks * L.args.NB;
+  const FmhaArgs& a = L.args;
+  if (a.NB > kMaxKeyBlocks || a.dense_start < 0 || a.dense_start > a.NB || a.dense_start > a.nB) return kErrShape;
+  const int grid = fmha_grid(a.banks, a.NB, a.dense_start, a.all_blocks);
   if (grid <= 0) return kOk;
   if (L.D == 128) {
     const int smem = FmhaSmem<128>::kTotal + 1024;
     cudaFuncSetAttribute(fmha_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    fmha_fwd_kernel<128><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.args);
+    fmha_fwd_kernel<128><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, a);
   } else if (L.D == 64) {
     // request enough shared memory for one CTA per SM (TMEM holds one CTA's 512 columns)
     int smem = FmhaSmem<64>::kTotal + 1024;
     if (smem < 120 * 1024) smem = 120 * 1024;
     cudaFuncSetAttribute(fmha_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    fmha_fwd_kernel<64><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.args);
+    fmha_fwd_kernel<64><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, a);
   } else {
     return kErrShape;
   }
