@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define RECAP_B200_ABI_VERSION 2
+#define RECAP_B200_ABI_VERSION 3
 
 #define RECAP_OK 0
 #define RECAP_ERR_SHAPE 1
@@ -196,6 +196,13 @@ int recap_refresh_detail_noalloc(const void* full_o, const float* full_lse, cons
                                  const int32_t* perm, int banks, int S, int D, int n_video, int video_offset,
                                  void* detail_value, float* detail_log_mass, int validate, const float* old_lse,
                                  const float* center, float* stats, void* stream);
+
+/* Self-check of the polynomial exponential the attention softmax uses for part of
+ * every row (2^y on the FP32 pipe, relative error below 1e-4 for -125 <= y <= 127;
+ * y < -125 gives 2^-125 in place of zero): out[i] = 2^in[i] for n values.  No
+ * counterpart in the reference; tests compare it with the CUDA exp2f of the same
+ * inputs. */
+int recap_exp2_check(const float* in, float* out, int n, void* stream);
 
 #ifdef __cplusplus
 }

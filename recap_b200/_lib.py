@@ -16,7 +16,7 @@ import torch
 PACKAGE_DIR = Path(__file__).resolve().parent
 LIB_PATH = PACKAGE_DIR / "librecap_b200.so"
 
-ABI_VERSION = 2  # RECAP_B200_ABI_VERSION of include/recap_b200.h
+ABI_VERSION = 3  # RECAP_B200_ABI_VERSION of include/recap_b200.h
 
 RECAP_OK = 0
 RECAP_ERR_SHAPE = 1
@@ -57,6 +57,7 @@ SIGNATURES: dict[str, tuple] = {
     "recap_refresh_partials": (_I, [_I, _I]),
     "recap_refresh_detail": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
     "recap_refresh_detail_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
+    "recap_exp2_check": (_I, [_P, _P, _I, _P]),
 }
 
 _lib = None

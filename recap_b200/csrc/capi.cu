@@ -331,6 +331,10 @@ int recap_sparse_step(const void* q_reordered, const void* k_reordered, const vo
   return launch_fmha(L, static_cast<cudaStream_t>(stream));
 }
 
+int recap_exp2_check(const float* in, float* out, int n, void* stream) {
+  return launch_exp2_check(in, out, n, static_cast<cudaStream_t>(stream));
+}
+
 int recap_refresh_partials(int banks, int n_video) {
   return refresh_partials_count(banks, (n_video / 128) * 128);
 }

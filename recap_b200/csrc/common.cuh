@@ -297,6 +297,23 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       : "memory");
 }
 
+// Load / store 8 consecutive fp32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+               : "memory");
+}
+
 // Store 16 consecutive 32-bit columns of this warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
@@ -344,6 +361,41 @@ __device__ __forceinline__ void mul2(float& d0, float& d1, float s0, float s1) {
       "mul.f32x2 rd, rd, ra;\n\tmov.b64 {%0, %1}, rd;\n\t}"
       : "+f"(d0), "+f"(d1)
       : "f"(s0), "f"(s1));
+}
+
+__device__ __forceinline__ void sub2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// 2^y for two values on the FP32 pipe instead of the MUFU unit (which computes only 16
+// exponentials per clock per SM): round-to-nearest range reduction y = n + f with
+// |f| <= 1/2 (adding 1.5 * 2^23 leaves n in the low mantissa bits), a degree-3 minimax
+// polynomial for 2^f (coefficients fitted here by linear programming over the relative
+// error on [-1/2, 1/2]; max relative error 7.5e-5), and 2^n applied by adding n to the
+// exponent field.  y is clamped to >= -125 so that the result stays a normal number;
+// there 2^y is below 2.4e-38 and stands for zero.  Valid for y <= 127.
+__device__ __forceinline__ void exp2_poly2(float& p0, float& p1, float y0, float y1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.9999280571937561f, c1 = 0.6932609677314758f, c2 = 0.24261131882667542f,
+                  c3 = 0.055171750485897064f;
+  y0 = fmaxf(y0, -125.0f);
+  y1 = fmaxf(y1, -125.0f);
+  float t0, t1, n0, n1, f0, f1;
+  t0 = y0;
+  t1 = y1;
+  add2(t0, t1, kRound, kRound);
+  sub2(n0, n1, t0, t1, kRound, kRound);
+  sub2(f0, f1, y0, y1, n0, n1);
+  float q0, q1;
+  fma2(q0, q1, c3, c3, f0, f1, c2, c2);
+  fma2(q0, q1, q0, q1, f0, f1, c1, c1);
+  fma2(q0, q1, q0, q1, f0, f1, c0, c0);
+  p0 = __uint_as_float(__float_as_uint(t0) * 8388608u + __float_as_uint(q0));
+  p1 = __uint_as_float(__float_as_uint(t1) * 8388608u + __float_as_uint(q1));
 }
 
 // max(a, b, c) in one instruction.

@@ -41,6 +41,11 @@ constexpr int kThreads = 320;
 constexpr int kSoftmaxWarp0 = 2;
 constexpr int kMaxKeyBlocks = 2048;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by 2^8
+// Of the 16 column pairs of every 32-key chunk, the ones whose bit is set here take
+// their exponentials from exp2_poly2 on the FP32 pipe instead of the MUFU unit.  Off:
+// with one softmax warp per SM sub-partition and tile the extra FP32 instructions
+// cost more than the MUFU time they free (measured on the bench workload).
+constexpr uint32_t kPolyPairs = 0x0u;
 
 template <int D>
 struct FmhaSmem {
@@ -410,8 +415,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) {
           float y0, y1;
           fma2(y0, y1, s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1], scale_log2, scale_log2, neg_m, neg_m);
-          const float p0 = fast_exp2(y0);
-          const float p1 = fast_exp2(y1);
+          float p0, p1;
+          if ((kPolyPairs >> i) & 1u) {
+            exp2_poly2(p0, p1, y0, y1);
+          } else {
+            p0 = fast_exp2(y0);
+            p1 = fast_exp2(y1);
+          }
           add2(sum[(i & 1) * 2], sum[(i & 1) * 2 + 1], p0, p1);
           pk[i] = pack_bf16(p0, p1);
         }
@@ -529,7 +539,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+__global__ void exp2_check_kernel(const float* in, float* out, int n) {
+  const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const float y0 = in[i];
+  const float y1 = i + 1 < n ? in[i + 1] : 0.f;
+  float p0, p1;
+  exp2_poly2(p0, p1, y0, y1);
+  out[i] = p0;
+  if (i + 1 < n) out[i + 1] = p1;
+}
+
 }  // namespace
+
+int launch_exp2_check(const float* in, float* out, int n, cudaStream_t stream) {
+  if (n <= 0) return n == 0 ? kOk : kErrShape;
+  if (in == nullptr || out == nullptr) return kErrShape;
+  const int pairs = (n + 1) / 2;
+  exp2_check_kernel<<<(pairs + 255) / 256, 256, 0, stream>>>(in, out, n);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
 
 int launch_fmha(const FmhaLaunch& L, cudaStream_t stream) {
   const FmhaArgs& a = L.args;

@@ -157,6 +157,8 @@ struct FmhaLaunch {
   FmhaArgs args;
 };
 int launch_fmha(const FmhaLaunch& L, cudaStream_t s);
+// out[i] = exp2_poly2(in[i]) (the softmax's FP32-pipe exponential)
+int launch_exp2_check(const float* in, float* out, int n, cudaStream_t s);
 
 // ------------------------------------------------------------------ refresh
 struct RefreshArgs {

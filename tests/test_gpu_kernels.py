@@ -182,6 +182,53 @@ def test_fmha_block_sparse_vs_oracle(d, nv, text, text_first):
     assert lerr <= 2e-3, f"LSE max abs err {lerr}"
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_fmha_uneven_pairs_vs_oracle(d):
+    """Query blocks are processed in pairs whose kept lists are split into blocks both keep
+    and blocks only one keeps; per-row densities from a single block to every block make
+    the two lists of a pair differ in length and run the shared-tile ring through many
+    wraps.  An odd block count leaves one CTA with a single query block."""
+    nv, text = 128 * 22 + 50, 60
+    lay = _layout(nv, text, False)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=14)
+    _, inp = _run_gather(lay, q, k, v, q_mean=False)
+    sh = inp.shapes
+    g = torch.Generator().manual_seed(15)
+    dens = torch.rand(sh.banks, sh.nB, 1, generator=g)
+    dens[:, ::5] = 0.0  # rows that keep only the forced blocks
+    dens[:, 3::7] = 1.0  # rows that keep everything
+    part = torch.rand(sh.banks, sh.nB, sh.nB, generator=g) < dens
+    part[:, -1, :] = True
+    part[:, :, -1] = True
+    out, lse = _fmha(inp.q, inp.k, inp.v_t, part.to(DEV), sh.banks, sh.S, d, nv, False)
+    kmask = orc.kernel_block_mask(part, sh.S, nv)
+    ro, rl = orc.masked_attention(inp.q[:, : sh.S].float().cpu(), inp.k[:, : sh.S].float().cpu(),
+                                  inp.v_t[:, :, : sh.S].transpose(1, 2).float().cpu(), kmask, 1 / math.sqrt(d))
+    err = (out.float().cpu() - ro).abs().max().item()
+    assert err <= 2e-2, f"O max abs err {err}"
+    lerr = (lse.cpu() - rl).abs().max().item()
+    assert lerr <= 2e-3, f"LSE max abs err {lerr}"
+
+
+def test_exp2_poly_vs_exp2f():
+    """The softmax's FP32-pipe exponential against exp2 in double precision on the GPU:
+    relative error below 1e-4 over the range it is used on, and a non-negative value below
+    2^-124 under it (where it stands for zero)."""
+    lib = _lib()
+    y = torch.cat([torch.linspace(-125.0, 127.0, 200001), torch.linspace(-8.0, 8.0, 100001),
+                   torch.tensor([0.0, -0.5, 0.5, -1e-7, 1e-7, -124.999, 126.9])]).to(DEV)
+    out = torch.empty_like(y)
+    lib.call("recap_exp2_check", lib.ptr(y), lib.ptr(out), y.numel(), lib.stream_handle(torch.device(DEV)))
+    ref = torch.exp2(y.double())
+    rel = ((out.double() - ref).abs() / ref).max().item()
+    assert rel <= 1e-4, rel
+    low = torch.tensor([-126.0, -200.0, -1e30, float("-inf")], device=DEV)
+    out_low = torch.empty_like(low)
+    lib.call("recap_exp2_check", lib.ptr(low), lib.ptr(out_low), low.numel(), lib.stream_handle(torch.device(DEV)))
+    torch.cuda.synchronize()
+    assert bool((out_low >= 0).all()) and float(out_low.max()) <= 2.0 ** -124
+
+
 def test_fmha_native_output_positions():
     nv, text, d = 700, 50, 64
     lay = _layout(nv, text, True)
