@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define RECAP_B200_ABI_VERSION 3
+#define RECAP_B200_ABI_VERSION 4
 
 #define RECAP_OK 0
 #define RECAP_ERR_SHAPE 1
@@ -134,11 +134,15 @@ int recap_basis_prep(const float* basis, int banks, int D, void* basis_t_bf16, v
  *   out            [banks, rows, D] bf16: coarse output + gate * drift
  *   lse            [banks, rows] fp32
  *   old_lse        [banks, rows] fp32 coarse LSE of the last refresh (nullable); with it,
- *                  center [banks] = mean(lse - old_lse) using center_partial [banks, rows/128]. */
+ *                  center [banks] = mean(lse - old_lse) using center_partial [banks, rows/128].
+ *   rank           the closure rank variance_bf16 is folded at (its columns >= rank hold
+ *                  one value, recap/sparse/closure.py:96-104); 0: not folded.  A folded
+ *                  variance lets the quadratic term run over rank + 2 columns.
+ * nB_pad must not exceed 2048. */
 int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const void* cvk_bf16,
                       const void* k_mean_bf16, const void* variance_bf16, const void* v_mean_t_bf16,
                       const uint8_t* partition, const float* counts_log, const float* old_lse, int banks,
-                      int S, int D, int n_video, float scale, float theta, void* out, float* lse,
+                      int S, int D, int n_video, float scale, float theta, int rank, void* out, float* lse,
                       float* center_partial, float* center, int* status, void* stream);
 
 /* Exact attention over the kept 128x128 tiles, with the natural-log LSE per row.

@@ -211,7 +211,7 @@ int recap_basis_prep(const float* basis, int banks, int D, void* basis_t_bf16, v
 int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const void* cvk_bf16,
                       const void* k_mean_bf16, const void* variance_bf16, const void* v_mean_t_bf16,
                       const uint8_t* partition, const float* counts_log, const float* old_lse, int banks,
-                      int S, int D, int n_video, float scale, float theta, void* out, float* lse,
+                      int S, int D, int n_video, float scale, float theta, int rank, void* out, float* lse,
                       float* center_partial, float* center, int* status, void* stream) {
   Geom g;
   if (!geom(S, n_video, &g) || !d_ok(D) || banks <= 0) return kErrShape;
@@ -222,8 +222,8 @@ int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const v
   rc |= make_tmap_bf16(&L.tm_q, q_reordered, static_cast<uint64_t>(banks) * g.S_pad, D, 128);
   rc |= make_tmap_bf16(&L.tm_basis_t, basis_t_bf16, static_cast<uint64_t>(banks) * D, D, D);
   rc |= make_tmap_bf16(&L.tm_cvk, cvk_bf16, static_cast<uint64_t>(banks) * D, D, D);
-  rc |= make_tmap_bf16(&L.tm_kmean, k_mean_bf16, static_cast<uint64_t>(banks) * g.nB_pad, D, 64);
-  rc |= make_tmap_bf16(&L.tm_var, variance_bf16, static_cast<uint64_t>(banks) * g.nB_pad, D, 64);
+  rc |= make_tmap_bf16(&L.tm_kmean, k_mean_bf16, static_cast<uint64_t>(banks) * g.nB_pad, D, 128);
+  rc |= make_tmap_bf16(&L.tm_var, variance_bf16, static_cast<uint64_t>(banks) * g.nB_pad, D, 128);
   rc |= make_tmap_bf16(&L.tm_vmean_t, v_mean_t_bf16, static_cast<uint64_t>(banks) * D, g.nB_pad, D);
   if (rc != kOk) return kErrShape;
   CoarseArgs& a = L.args;
@@ -236,6 +236,7 @@ int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const v
   a.n_video = n_video;
   a.scale = scale;
   a.theta = theta;
+  a.rank = rank < 0 || rank >= D ? 0 : rank;
   a.partition = partition;
   a.counts_log = counts_log;
   a.old_lse = old_lse;

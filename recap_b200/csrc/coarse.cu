@@ -7,20 +7,34 @@
 // (_coarse_tail_kernel, recap/kernels/coarse_tail.py:36-186, and its wrapper
 // 194-312).  qsq = (Q U)^2 and drift = s Q C_vk^T (rotated_query_square and
 // value_drift, recap/sparse/closure.py:84-93) are computed here from the Q tile
-// with two tcgen05 MMAs and never reach HBM.  Rounding follows the reference:
-// kbar, vbar, w, U and C_vk in bf16, qsq and drift rounded to bf16 as the bf16
-// bmm outputs they replace, P rounded to bf16 before P vbar, the output rounded
-// to bf16 and the drift added in bf16 arithmetic.
+// with tcgen05 MMAs and never reach HBM.  Rounding follows the reference: kbar,
+// vbar, w, U and C_vk in bf16, qsq and drift rounded to bf16 as the bf16 bmm outputs
+// they replace, P rounded to bf16 before P vbar, the output rounded to bf16 and the
+// drift added in bf16 arithmetic.
 //
-// The omitted set is a mask over all nB block means, processed in 64-column tiles
-// (kbar, w and vbar^T of a bank stay in L2).  One CTA per (query block, bank), 8 warps:
-//   warp 0      TMA producer: Q, U^T and C_vk once, then (kbar, w, vbar^T) tiles
-//               through a 2-stage ring;
-//   warp 1      TMEM allocator and MMA issuer: Q U and Q C_vk^T, then per tile
-//               S1 = Q kbar^T and S2 = qsq w^T into one of two TMEM buffer pairs,
-//               and O += P vbar;
-//   warps 4-7   one query row per thread: qsq, the gated online softmax (log2 domain,
-//               lazy rescaling of O), P in shared memory, the epilogue.
+// Rank folding: with 0 < rank and rank + 2 <= 64, the per-block variances w_j are
+// folded (recap/sparse/closure.py:96-104): every column c >= rank holds the same tail
+// value.  Then  qsq . w_j = sum_{c<rank} qsq_c w_jc + w_j,rank * T  with
+// T = sum_{c>=rank} qsq_c, and the quadratic term is one MMA over K = 16 (rank <= 14):
+// the A row is (qsq_0 .. qsq_{rank-1}, T_hi, T_lo, 0 ...) with T split into two bf16
+// parts (T_hi + T_lo = T to 2^-17), the B row the first 16 folded columns of w_j.
+// Otherwise the product runs over all D columns.
+//
+// The omitted set is a mask over all nB block means, processed in tiles of 128
+// (kbar, w and vbar^T of a bank stay in L2).  One CTA per (query block, bank),
+// 8 warps:
+//   warp 0      TMA producer of Q, U^T (prologue), the (kbar, w) tiles and C_vk;
+//   warp 1      TMEM allocator and MMA issuer;
+//   warp 2      TMA producer of the vbar^T tiles;
+//   warps 4-7   one query row per thread: qsq, the gated online softmax (log2
+//               domain, lazy rescaling of O), P into TMEM, the epilogue.
+// TMEM: S1 = Q kbar^T double-buffered in columns [0,128) and [128,256), S2 = qsq w^T
+// in [256,384), O in [384,384+D).  Q U goes to the O columns before the first P.V,
+// and the drift Q C_vk^T to the S2 columns after the last S2 has been read.  P
+// (bf16) overwrites the first 64 columns of its S1 buffer and is the A operand of
+// O += P vbar from TMEM; S1(j+2) reuses that buffer only after P.V(j), issued
+// before it by the same thread.  The softmax reads S2(j) first and releases it, so
+// S2(j+1) and the products of the previous tile run while it computes.
 // The epilogue also writes the per-block sum of (lse - old_lse) for the drift centre
 // (recap/operator.py:148-150).
 #include "common.cuh"
@@ -31,66 +45,80 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kSoftmaxWarp0 = 4;
-constexpr int kTileN = 64;          // block means per tile
-constexpr int kStages = 2;
-constexpr int kMaxBlocks = 4096;    // nB_pad limit (column terms in shared memory)
+constexpr int kTileN = 128;         // block means per tile
+constexpr int kMaxBlocks = 2048;    // nB_pad limit (column terms in shared memory)
 constexpr float kRescaleThreshold = 8.0f;
+constexpr float kLog2e = 1.4426950408889634f;
 
-template <int D>
+// FOLD: the quadratic term over K = 16 * k2 <= 64 (one 64-column atom of w);
+// otherwise over all D columns.
+template <int D, bool FOLD>
 struct CoarseSmem {
   static constexpr int kTileQ = 128 * D * 2;
-  static constexpr int kOpK = kTileN * D * 2;      // kbar tile: 64 rows x D
-  static constexpr int kOpW = kTileN * D * 2;      // w tile
-  static constexpr int kOpV = D * kTileN * 2;      // vbar^T tile: D rows x 64
-  static constexpr int kStage = kOpK + kOpW + kOpV;
+  static constexpr int kQsqBytes = FOLD ? 128 * 128 : kTileQ;  // A operand of S2
+  static constexpr int kOpK = kTileN * D * 2;                  // kbar tile: 128 rows x D
+  static constexpr int kOpW = FOLD ? kTileN * 128 : kTileN * D * 2;
+  static constexpr int kKW = kOpK + kOpW;                      // one (kbar, w) stage
+  static constexpr int kOpV = D * kTileN * 2;                  // one vbar^T stage: D rows x 128
+  static constexpr int kKWStages = (D == 128 && !FOLD) ? 1 : 2;
+  static constexpr int kVStages = 2;
   static constexpr int kQ = 0;
   static constexpr int kQsq = kQ + kTileQ;
-  static constexpr int kP = kQsq + kTileQ;         // 128 x 64 bf16, one swizzle atom
-  static constexpr int kRing = kP + 128 * kTileN * 2;
-  // U^T (D x D) and C_vk (D x D) share the ring before the first tile
-  static constexpr int kRingBytes = (kStages * kStage > 2 * D * D * 2) ? kStages * kStage : 2 * D * D * 2;
-  static constexpr int kCol = kRing + kRingBytes;  // fp32 column terms [kMaxBlocks]
+  static constexpr int kKWRing = kQsq + kQsqBytes;
+  static constexpr int kVRing = kKWRing + kKWStages * kKW;
+  static constexpr int kCol = kVRing + kVStages * kOpV;       // fp32 column terms [kMaxBlocks]
   static constexpr int kBars = kCol + kMaxBlocks * 4;
-  // bars: pro_full, pro_done, qsq_ready, full[2], empty[2], sfull[2], sfree[2], pfull, ofull, done
-  static constexpr int kNumBars = 3 + 4 * kStages + 3 + 2;
+  // pro_full, pro_mma, qsq_ready, kw_full[2], kw_empty[2], v_full[2], v_empty[2],
+  // s1full[2], s2full, s2free, pfull, ofull, c_full, xfull, done
+  static constexpr int kNumBars = 3 + 8 + 2 + 8;
   static constexpr int kMisc = kBars + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16 + 4 * 4;
+  static_assert(kOpV >= D * D * 2, "U^T is staged in a vbar^T slot");
+  static_assert(kKW >= D * D * 2, "C_vk is staged in a (kbar, w) slot");
 };
 
 struct CoarseBars {
-  uint64_t *pro_full, *pro_done, *qsq_ready, *full, *empty, *sfull, *sfree, *pfull, *ofull, *done;
+  uint64_t *pro_full, *pro_mma, *qsq_ready, *kw_full, *kw_empty, *v_full, *v_empty, *s1full, *s2full, *s2free,
+      *pfull, *ofull, *c_full, *xfull, *done;
 };
 
 __device__ __forceinline__ CoarseBars carve(uint8_t* base) {
   uint64_t* b = reinterpret_cast<uint64_t*>(base);
   CoarseBars r;
   r.pro_full = b;
-  r.pro_done = b + 1;
+  r.pro_mma = b + 1;
   r.qsq_ready = b + 2;
-  r.full = b + 3;
-  r.empty = b + 3 + kStages;
-  r.sfull = b + 3 + 2 * kStages;
-  r.sfree = b + 3 + 3 * kStages;
-  r.pfull = b + 3 + 4 * kStages;
-  r.ofull = b + 4 + 4 * kStages;
-  r.done = b + 5 + 4 * kStages;
+  r.kw_full = b + 3;
+  r.kw_empty = b + 5;
+  r.v_full = b + 7;
+  r.v_empty = b + 9;
+  r.s1full = b + 11;
+  r.s2full = b + 13;
+  r.s2free = b + 14;
+  r.pfull = b + 15;
+  r.ofull = b + 16;
+  r.c_full = b + 17;
+  r.xfull = b + 18;
+  r.done = b + 19;
   return r;
 }
 
-template <int D>
+template <int D, bool FOLD>
 __global__ void __launch_bounds__(kThreads, 1)
     coarse_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ut,
                   const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_kbar,
                   const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_vbt,
                   const CoarseArgs a) {
-  using L = CoarseSmem<D>;
+  using L = CoarseSmem<D, FOLD>;
+  constexpr int KWS = L::kKWStages;
+  constexpr int VS = L::kVStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem + L::kQ;
   uint8_t* sQsq = smem + L::kQsq;
-  uint8_t* sP = smem + L::kP;
-  uint8_t* sRing = smem + L::kRing;
+  uint8_t* sKW = smem + L::kKWRing;
+  uint8_t* sV = smem + L::kVRing;
   float* colterm = reinterpret_cast<float*>(smem + L::kCol);
   CoarseBars bars = carve(smem + L::kBars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
@@ -103,133 +131,220 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int nB = a.nB;
   const int n_tiles = a.nB_pad / kTileN;
+  // K-steps of the quadratic term
+  const int k2 = FOLD ? (a.rank + 2 + 15) / 16 : D / 16;
 
   if (threadIdx.x == 0) {
     mbar_init(bars.pro_full, 1);
-    mbar_init(bars.pro_done, 1);
+    mbar_init(bars.pro_mma, 1);
     mbar_init(bars.qsq_ready, 4);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bars.full + s, 1);
-      mbar_init(bars.empty + s, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bars.kw_full + s, 1);
+      mbar_init(bars.kw_empty + s, 1);
+      mbar_init(bars.v_full + s, 1);
+      mbar_init(bars.v_empty + s, 1);
+      mbar_init(bars.s1full + s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bars.sfull + b, 1);
-      mbar_init(bars.sfree + b, 4);
-    }
+    mbar_init(bars.s2full, 1);
+    mbar_init(bars.s2free, 4);
     mbar_init(bars.pfull, 4);
     mbar_init(bars.ofull, 1);
+    mbar_init(bars.c_full, 1);
+    mbar_init(bars.xfull, 1);
     mbar_init(bars.done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   {
-    // per-column term: ln n_j for omitted blocks, -inf for selected or padding ones
+    // per-column term (log2 units): ln n_j for omitted blocks, -inf for kept or padding
     const uint8_t* prow = a.partition + (static_cast<size_t>(bank) * nB + qb) * nB;
     for (int j = threadIdx.x; j < a.nB_pad; j += kThreads)
-      colterm[j] = (j < nB && prow[j] == 0) ? a.counts_log[j] : -INFINITY;
+      colterm[j] = (j < nB && prow[j] == 0) ? a.counts_log[j] * kLog2e : -INFINITY;
   }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s1 = tmem;          // S1 buffers: columns [0,64) and [64,128); Q U in [0, D)
-  const uint32_t t_s2 = tmem + 128;    // S2 buffers: columns [128,192) and [192,256)
-  const uint32_t t_o = tmem + 256;     // O: columns [256, 256 + D)
-  const uint32_t t_x = tmem + 384;     // Q C_vk^T: columns [384, 384 + D)
+  const uint32_t t_s1 = tmem;          // two S1 buffers (P aliases their first 64 columns)
+  const uint32_t t_s2 = tmem + 256;    // S2; the drift at the end
+  const uint32_t t_o = tmem + 384;     // O; Q U in the prologue
   constexpr uint32_t kTileQ = L::kTileQ;
 
   if (warp == 0) {
-    // ================================================================ producer
+    // ================================================================ Q, U^T, (kbar, w), C_vk
     if (lane == 0) {
       const uint64_t keep = l2_evict_last();    // per-bank operands: read by every query block
       const uint64_t stream = l2_evict_first(); // the Q tile: read once here
       const int qrow = bank * a.S_pad + qb * 128;
-      mbar_expect_tx(bars.pro_full, kTileQ + 2 * D * D * 2);
+      mbar_expect_tx(bars.pro_full, kTileQ + D * D * 2);
 #pragma unroll
       for (int at = 0; at < D / 64; ++at) {
         tma_load_2d_hint(sQ + at * 128 * 128, &tm_q, bars.pro_full, at * 64, qrow, stream);
-        tma_load_2d(sRing + at * D * 128, &tm_ut, bars.pro_full, at * 64, bank * D);
-        tma_load_2d(sRing + D * D * 2 + at * D * 128, &tm_c, bars.pro_full, at * 64, bank * D);
+        // U^T waits in the second vbar^T slot, which the second tile needs last
+        tma_load_2d(sV + (1 % VS) * L::kOpV + at * D * 128, &tm_ut, bars.pro_full, at * 64, bank * D);
       }
-      // the ring holds U^T and C_vk until the prologue MMAs have read them
-      bool ok = mbar_wait(bars.pro_done, 0, abort_flag, a.status, kStatusTimeoutProducer);
+      bool ok = true;
       int j = 0;
       for (; ok && j < n_tiles; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages &&
-            !mbar_wait(bars.empty + st, ((j / kStages) - 1) & 1, abort_flag, a.status, kStatusTimeoutProducer))
+        const int st = j % KWS;
+        if (j >= KWS &&
+            !mbar_wait(bars.kw_empty + st, ((j / KWS) - 1) & 1, abort_flag, a.status, kStatusTimeoutProducer)) {
+          ok = false;
           break;
-        uint8_t* base = sRing + st * L::kStage;
-        const int brow = bank * a.nB_pad + j * kTileN;
-        mbar_expect_tx(bars.full + st, L::kStage);
-#pragma unroll
-        for (int at = 0; at < D / 64; ++at) {
-          tma_load_2d_hint(base + at * kTileN * 128, &tm_kbar, bars.full + st, at * 64, brow, keep);
-          tma_load_2d_hint(base + L::kOpK + at * kTileN * 128, &tm_w, bars.full + st, at * 64, brow, keep);
         }
-        tma_load_2d_hint(base + L::kOpK + L::kOpW, &tm_vbt, bars.full + st, j * kTileN, bank * D, keep);
+        uint8_t* base = sKW + st * L::kKW;
+        const int brow = bank * a.nB_pad + j * kTileN;
+        mbar_expect_tx(bars.kw_full + st, L::kKW);
+#pragma unroll
+        for (int at = 0; at < D / 64; ++at)
+          tma_load_2d_hint(base + at * kTileN * 128, &tm_kbar, bars.kw_full + st, at * 64, brow, keep);
+#pragma unroll
+        for (int at = 0; at < (FOLD ? 1 : D / 64); ++at)
+          tma_load_2d_hint(base + L::kOpK + at * kTileN * 128, &tm_w, bars.kw_full + st, at * 64, brow, keep);
       }
-      const int first = j > kStages ? j - kStages : 0;
-      for (int k = first; k < j; ++k) mbar_drain(bars.full + (k % kStages), (k / kStages) & 1);
+      // C_vk into the (kbar, w) slot that the tile after the last would use
+      int loads = j;
+      if (ok) {
+        const int st = n_tiles % KWS;
+        if (n_tiles >= KWS &&
+            !mbar_wait(bars.kw_empty + st, ((n_tiles / KWS) - 1) & 1, abort_flag, a.status, kStatusTimeoutProducer))
+          ok = false;
+        if (ok) {
+          mbar_expect_tx(bars.c_full, D * D * 2);
+#pragma unroll
+          for (int at = 0; at < D / 64; ++at)
+            tma_load_2d(sKW + st * L::kKW + at * D * 128, &tm_c, bars.c_full, at * 64, bank * D);
+          mbar_drain(bars.c_full, 0);
+        }
+      }
+      const int first = loads > KWS ? loads - KWS : 0;
+      for (int k = first; k < loads; ++k) mbar_drain(bars.kw_full + (k % KWS), (k / KWS) & 1);
       mbar_drain(bars.pro_full, 0);
+    }
+  } else if (warp == 2) {
+    // ================================================================ vbar^T tiles
+    if (lane == 0) {
+      const uint64_t keep = l2_evict_last();
+      bool ok = true;
+      int j = 0;
+      for (; ok && j < n_tiles; ++j) {
+        const int st = j % VS;
+        if (j >= VS) {
+          ok = mbar_wait(bars.v_empty + st, ((j / VS) - 1) & 1, abort_flag, a.status, kStatusTimeoutProducer);
+        } else if (st == 1 % VS) {
+          // the slot still holds U^T until the prologue MMA has read it
+          ok = mbar_wait(bars.pro_mma, 0, abort_flag, a.status, kStatusTimeoutProducer);
+        }
+        if (!ok) break;
+        uint8_t* base = sV + st * L::kOpV;
+        mbar_expect_tx(bars.v_full + st, L::kOpV);
+#pragma unroll
+        for (int at = 0; at < kTileN / 64; ++at)
+          tma_load_2d_hint(base + at * D * 128, &tm_vbt, bars.v_full + st, j * kTileN + at * 64, bank * D, keep);
+      }
+      const int first = j > VS ? j - VS : 0;
+      for (int k = first; k < j; ++k) mbar_drain(bars.v_full + (k % VS), (k / VS) & 1);
     }
   } else if (warp == 1) {
     // ================================================================ MMA issuer
     if (lane == 0) {
-      const uint32_t q0 = smem_u32(sQ), qs0 = smem_u32(sQsq), p0 = smem_u32(sP), ring = smem_u32(sRing);
-      bool ok = mbar_wait(bars.pro_full, 0, abort_flag, a.status, kStatusTimeoutTma);
+      const uint32_t q0 = smem_u32(sQ), qs0 = smem_u32(sQsq), kw0 = smem_u32(sKW), v0 = smem_u32(sV);
+      auto wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+        return mbar_wait(bar, parity, abort_flag, a.status, code);
+      };
+      bool ok = wait(bars.pro_full, 0, kStatusTimeoutTma);
       if (ok) {
+        // Q U into the O columns
         tc_fence_after();
         constexpr uint32_t idesc = idesc_bf16_f32(128, D);
+        const uint32_t ut = v0 + (1 % VS) * L::kOpV;
 #pragma unroll
         for (int s = 0; s < D / 16; ++s) {
           const uint32_t offq = (s >> 2) * (128 * 128) + (s & 3) * 32;
           const uint32_t offb = (s >> 2) * (D * 128) + (s & 3) * 32;
-          mma_bf16_ss(t_s1, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(ring + offb), idesc, s > 0);
-          mma_bf16_ss(t_x, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(ring + D * D * 2 + offb), idesc, s > 0);
+          mma_bf16_ss(t_o, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(ut + offb), idesc, s > 0);
         }
-        mma_commit(bars.pro_done);
-        ok = mbar_wait(bars.qsq_ready, 0, abort_flag, a.status, kStatusTimeoutMma);
+        mma_commit(bars.pro_mma);
       }
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % kStages;
-        if (!mbar_wait(bars.full + st, (j / kStages) & 1, abort_flag, a.status, kStatusTimeoutTma)) return false;
-        const int b = j & 1;
-        if (j >= 2 && !mbar_wait(bars.sfree + b, ((j >> 1) - 1) & 1, abort_flag, a.status, kStatusTimeoutMma))
-          return false;
+      auto issue_s1 = [&](int j) -> bool {
+        const int st = j % KWS;
+        if (!wait(bars.kw_full + st, (j / KWS) & 1, kStatusTimeoutTma)) return false;
         tc_fence_after();
         constexpr uint32_t idesc = idesc_bf16_f32(128, kTileN);
-        const uint32_t kb = ring + st * L::kStage;
-        const uint32_t wb = kb + L::kOpK;
+        const uint32_t kb = kw0 + st * L::kKW;
 #pragma unroll
         for (int s = 0; s < D / 16; ++s) {
           const uint32_t offq = (s >> 2) * (128 * 128) + (s & 3) * 32;
           const uint32_t offb = (s >> 2) * (kTileN * 128) + (s & 3) * 32;
-          mma_bf16_ss(t_s1 + b * kTileN, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(kb + offb), idesc, s > 0);
-          mma_bf16_ss(t_s2 + b * kTileN, sdesc_k_sw128(qs0 + offq), sdesc_k_sw128(wb + offb), idesc, s > 0);
+          mma_bf16_ss(t_s1 + (j & 1) * kTileN, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(kb + offb), idesc, s > 0);
         }
-        mma_commit(bars.sfull + b);
+        mma_commit(bars.s1full + (j & 1));
+        return true;
+      };
+      // S2(j) reads the (kbar, w) slot of tile j last: release it afterwards
+      auto issue_s2 = [&](int j) -> bool {
+        const int st = j % KWS;
+        if (!wait(bars.kw_full + st, (j / KWS) & 1, kStatusTimeoutTma)) return false;
+        tc_fence_after();
+        constexpr uint32_t idesc = idesc_bf16_f32(128, kTileN);
+        const uint32_t wb = kw0 + st * L::kKW + L::kOpK;
+        for (int s = 0; s < k2; ++s) {
+          const uint32_t offq = (s >> 2) * (128 * 128) + (s & 3) * 32;
+          const uint32_t offb = (s >> 2) * (kTileN * 128) + (s & 3) * 32;
+          mma_bf16_ss(t_s2, sdesc_k_sw128(qs0 + offq), sdesc_k_sw128(wb + offb), idesc, s > 0);
+        }
+        mma_commit(bars.s2full);
+        mma_commit(bars.kw_empty + st);
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        if (!mbar_wait(bars.pfull, j & 1, abort_flag, a.status, kStatusTimeoutMma)) return false;
+        if (!wait(bars.pfull, j & 1, kStatusTimeoutMma)) return false;
+        const int st = j % VS;
+        if (!wait(bars.v_full + st, (j / VS) & 1, kStatusTimeoutTma)) return false;
         tc_fence_after();
-        const int st = j % kStages;
         constexpr uint32_t idesc = idesc_bf16_f32(128, D);
-        const uint32_t vb = ring + st * L::kStage + L::kOpK + L::kOpW;
+        const uint32_t vb = v0 + st * L::kOpV;
+        const uint32_t p = t_s1 + (j & 1) * kTileN;
 #pragma unroll
-        for (int s = 0; s < kTileN / 16; ++s)
-          mma_bf16_ss(t_o, sdesc_k_sw128(p0 + s * 32), sdesc_k_sw128(vb + s * 32), idesc, (j > 0 || s > 0) ? 1u : 0u);
-        mma_commit(bars.empty + st);
+        for (int s = 0; s < kTileN / 16; ++s) {
+          const uint32_t offv = (s >> 2) * (D * 128) + (s & 3) * 32;
+          mma_bf16_ts(t_o, p + 8 * s, sdesc_k_sw128(vb + offv), idesc, (j > 0 || s > 0) ? 1u : 0u);
+        }
         mma_commit(bars.ofull);
+        mma_commit(bars.v_empty + st);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 1; ok && j < n_tiles; ++j) {
-        ok = issue_s(j);
-        if (ok) ok = issue_pv(j - 1);
+      // S1 of the first tiles do not need qsq (the O columns hold Q U until then).  With
+      // one (kbar, w) slot the second tile's operands arrive only after S2(0) has read
+      // the first ones.
+      if (ok) ok = issue_s1(0);
+      if (ok && n_tiles > 1 && KWS > 1) ok = issue_s1(1);
+      if (ok) ok = wait(bars.qsq_ready, 0, kStatusTimeoutMma);
+      if (ok) ok = issue_s2(0);
+      if (ok && n_tiles > 1 && KWS == 1) ok = issue_s1(1);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles) {
+          ok = wait(bars.s2free, j & 1, kStatusTimeoutMma);
+          if (ok) ok = issue_s2(j + 1);
+        }
+        if (ok) ok = issue_pv(j);
+        if (ok && j + 2 < n_tiles) ok = issue_s1(j + 2);
       }
-      if (ok) ok = issue_pv(n_tiles - 1);
+      // drift: Q C_vk^T into the S2 columns once the last S2 has been read
+      if (ok) ok = wait(bars.s2free, (n_tiles - 1) & 1, kStatusTimeoutMma);
+      if (ok) ok = wait(bars.c_full, 0, kStatusTimeoutTma);
+      if (ok) {
+        tc_fence_after();
+        constexpr uint32_t idesc = idesc_bf16_f32(128, D);
+        const uint32_t cb = kw0 + (n_tiles % KWS) * L::kKW;
+#pragma unroll
+        for (int s = 0; s < D / 16; ++s) {
+          const uint32_t offq = (s >> 2) * (128 * 128) + (s & 3) * 32;
+          const uint32_t offb = (s >> 2) * (D * 128) + (s & 3) * 32;
+          mma_bf16_ss(t_s2, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(cb + offb), idesc, s > 0);
+        }
+        mma_commit(bars.xfull);
+      }
       mma_commit(bars.done);
       mbar_drain(bars.done, 0);
     }
@@ -238,34 +353,71 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = threadIdx.x - kSoftmaxWarp0 * 32;
     const int q4 = warp - kSoftmaxWarp0;
     const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
-    constexpr float kLog2e = 1.4426950408889634f;
     const float scale = a.scale;
-    const float s2 = scale * scale;
-    const float half_s2 = 0.5f * s2;
-    const float th2 = a.theta * a.theta;
-    bool ok = mbar_wait(bars.pro_done, 0, abort_flag, a.status, kStatusTimeoutSoftmax);
+    const float s_l2 = scale * kLog2e;                      // S1 -> log2 units
+    const float h_l2 = 0.5f * scale * scale * kLog2e;       // gated S2 -> log2 units
+    const float gate_max = a.theta * a.theta / (scale * scale);  // s^2 quad <= theta^2
+    bool ok = mbar_wait(bars.pro_mma, 0, abort_flag, a.status, kStatusTimeoutSoftmax);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       tc_fence_after();
-      // qsq = bf16(bf16(q U)^2), written as the K-major A operand of qsq . w^T
+      // qsq = bf16(bf16(q U)^2): the A operand of the quadratic term (row t, K-major,
+      // 128-byte swizzle)
       const uint32_t qsq_row = smem_u32(sQsq) + t * 128;
+      if (FOLD) {
+        // zero the row's 16 k2 columns, then (qsq_0 .. qsq_{rank-1}, T_hi, T_lo)
+        const int rank = a.rank;
+        for (int k = 0; k < 16 * k2; k += 8)
+          st_shared_v4(qsq_row + (((k >> 3) ^ (t & 7)) << 4), 0u, 0u, 0u, 0u);
+        float tail = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        tmem_ld32(t_s1 + c * 32 + lane_base, v);
-        tmem_wait_ld();
-        uint32_t pk[16];
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tmem_ld32(t_o + c * 32 + lane_base, v);
+          tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float x0 = bf16_round(v[2 * e]);
-          const float x1 = bf16_round(v[2 * e + 1]);
-          pk[e] = pack_bf16(x0 * x0, x1 * x1);
+          for (int e = 0; e < 32; ++e) {
+            const int k = c * 32 + e;
+            const float x = bf16_round(v[e]);
+            const float q2 = bf16_round(x * x);
+            if (k < rank) {
+              const __nv_bfloat16 h = __float2bfloat16_rn(q2);
+              asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k >> 3) ^ (t & 7)) << 4) + (k & 7) * 2),
+                           "h"(*reinterpret_cast<const unsigned short*>(&h))
+                           : "memory");
+            } else {
+              tail += q2;
+            }
+          }
         }
+        const __nv_bfloat16 hi = __float2bfloat16_rn(tail);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(tail - __bfloat162float(hi));
+        const int k_hi = rank, k_lo = rank + 1;
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_hi >> 3) ^ (t & 7)) << 4) + (k_hi & 7) * 2),
+                     "h"(*reinterpret_cast<const unsigned short*>(&hi))
+                     : "memory");
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_lo >> 3) ^ (t & 7)) << 4) + (k_lo & 7) * 2),
+                     "h"(*reinterpret_cast<const unsigned short*>(&lo))
+                     : "memory");
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tmem_ld32(t_o + c * 32 + lane_base, v);
+          tmem_wait_ld();
+          uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int k = c * 32 + q * 8;
-          st_shared_v4(qsq_row + (k >> 6) * 16384 + ((((k & 63) >> 3) ^ (t & 7)) << 4), pk[4 * q], pk[4 * q + 1],
-                       pk[4 * q + 2], pk[4 * q + 3]);
+          for (int e = 0; e < 16; ++e) {
+            const float x0 = bf16_round(v[2 * e]);
+            const float x1 = bf16_round(v[2 * e + 1]);
+            pk[e] = pack_bf16(x0 * x0, x1 * x1);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int k = c * 32 + q * 8;
+            st_shared_v4(qsq_row + (k >> 6) * 16384 + ((((k & 63) >> 3) ^ (t & 7)) << 4), pk[4 * q], pk[4 * q + 1],
+                         pk[4 * q + 2], pk[4 * q + 3]);
+          }
         }
       }
       fence_async_smem();
@@ -275,98 +427,108 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     float m_run = -INFINITY;  // running max (log2 domain)
     float l_run = 0.f, g_run = 0.f;
-    const uint32_t p_row = smem_u32(sP) + t * 128;
     for (int j = 0; ok && j < n_tiles; ++j) {
       const int b = j & 1;
-      ok = mbar_wait(bars.sfull + b, (j >> 1) & 1, abort_flag, a.status, kStatusTimeoutSoftmax);
+      ok = mbar_wait(bars.s1full + b, (j >> 1) & 1, abort_flag, a.status, kStatusTimeoutSoftmax);
+      if (ok) ok = mbar_wait(bars.s2full, j & 1, abort_flag, a.status, kStatusTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       float x[kTileN];
-      uint32_t gate[2];
+      uint32_t gate[4];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float v1[32], v2[32];
         tmem_ld32(t_s1 + b * kTileN + c * 32 + lane_base, v1);
-        tmem_ld32(t_s2 + b * kTileN + c * 32 + lane_base, v2);
+        tmem_ld32(t_s2 + c * 32 + lane_base, v2);
         tmem_wait_ld();
+        const float4* ct4 = reinterpret_cast<const float4*>(colterm + j * kTileN + c * 32);
         uint32_t gm = 0;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float quad = v2[e];
-          const bool gt = quad * s2 <= th2;
-          gm |= gt ? (1u << e) : 0u;
-          const float term = colterm[j * kTileN + c * 32 + e];
-          // natural-log logit, then into the log2 domain
-          const float sc = v1[e] * scale + term + (gt ? quad * half_s2 : 0.f);
-          x[c * 32 + e] = sc * kLog2e;
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const float4 ct = ct4[e4];
+          const float cts[4] = {ct.x, ct.y, ct.z, ct.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const int e = 4 * e4 + h;
+            const float quad = v2[e];
+            const bool gt = quad <= gate_max;
+            gm |= gt ? (1u << e) : 0u;
+            x[c * 32 + e] = fmaf(quad, gt ? h_l2 : 0.f, fmaf(v1[e], s_l2, cts[h]));
+          }
         }
-        gate[c] = gm;
+        // opaque copy: the exponential phase then tests these packed bits instead of the
+        // compiler keeping 32 comparison results per word alive (which spills)
+        asm volatile("mov.b32 %0, %1;" : "=r"(gate[c]) : "r"(gm));
       }
+      // S2 has been read: the next tile's quadratic term may overwrite it
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bars.sfree + b);
-      float mxa[8];
+      if (lane == 0) mbar_arrive(bars.s2free);
+      float mx[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mxa[k] = x[k];
+      for (int k = 0; k < 8; ++k) mx[k] = max3(x[k], x[8 + k], x[16 + k]);
 #pragma unroll
-      for (int i = 8; i < kTileN; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], x[i]);
-      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+      for (int i = 24; i < kTileN; i += 16) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], x[i + k], x[i + 8 + k]);
+      }
+      const float m_tile = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       float alpha = 1.f;
       bool rescale = false;
-      if (mx != -INFINITY) {
+      if (m_tile != -INFINITY) {
         if (m_run == -INFINITY) {
-          m_run = mx;
-        } else if (mx > m_run + kRescaleThreshold) {
-          alpha = fast_exp2(m_run - mx);
-          m_run = mx;
+          m_run = m_tile;  // nothing accumulated yet: O, l and g are zero
+        } else if (m_tile > m_run + kRescaleThreshold) {
+          alpha = fast_exp2(m_run - m_tile);
+          m_run = m_tile;
           rescale = true;
         }
       }
-      float ls[4] = {0.f, 0.f, 0.f, 0.f}, gs[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[kTileN / 2];
-#pragma unroll
-      for (int e = 0; e < kTileN / 2; ++e) {
-        const int c0 = 2 * e, c1 = 2 * e + 1;
-        const float p0 = x[c0] == -INFINITY ? 0.f : fast_exp2(x[c0] - m_run);
-        const float p1 = x[c1] == -INFINITY ? 0.f : fast_exp2(x[c1] - m_run);
-        ls[e & 3] += p0 + p1;
-        gs[e & 3] += (((gate[c0 >> 5] >> (c0 & 31)) & 1u) ? p0 : 0.f) + (((gate[c1 >> 5] >> (c1 & 31)) & 1u) ? p1 : 0.f);
-        pk[e] = pack_bf16(p0, p1);
-      }
-      const float lsum = (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      const float gsum = (gs[0] + gs[1]) + (gs[2] + gs[3]);
-      l_run = l_run * alpha + lsum;
-      g_run = g_run * alpha + gsum;
-      if (j > 0) {
+      // O must hold P.V(j-1) before it is rescaled; P.V(j) starts after pfull below
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
         ok = mbar_wait(bars.ofull, (j - 1) & 1, abort_flag, a.status, kStatusTimeoutSoftmax);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            float v[32];
-            tmem_ld32(t_o + c * 32 + lane_base, v);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 8; ++c) {
+          float o[8];
+          tmem_ld8(t_o + c * 8 + lane_base, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= alpha;
-            tmem_st32(t_o + c * 32 + lane_base, v);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 8; i += 2) mul2(o[i], o[i + 1], alpha, alpha);
+          tmem_st8(t_o + c * 8 + lane_base, o);
         }
       }
+      const float neg_m = m_run == -INFINITY ? 0.f : -m_run;  // exp2(-inf + 0) = 0
+      float ls[4] = {0.f, 0.f, 0.f, 0.f}, gs[2] = {0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < kTileN / 8; ++c)
-        st_shared_v4(p_row + ((c ^ (t & 7)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_async_smem();
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e0 = 2 * i, e1 = 2 * i + 1;
+          const float p0 = fast_exp2(x[c * 32 + e0] + neg_m);
+          const float p1 = fast_exp2(x[c * 32 + e1] + neg_m);
+          add2(ls[(i & 1) * 2], ls[(i & 1) * 2 + 1], p0, p1);
+          const float g0 = ((gate[c] >> e0) & 1u) ? p0 : 0.f;
+          const float g1 = ((gate[c] >> e1) & 1u) ? p1 : 0.f;
+          add2(gs[0], gs[1], g0, g1);
+          pk[i] = pack_bf16(p0, p1);
+        }
+        tmem_st16(t_s1 + b * kTileN + c * 16 + lane_base, pk);
+      }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bars.pfull);
+      l_run = l_run * alpha + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+      g_run = g_run * alpha + (gs[0] + gs[1]);
     }
     if (ok) {
       ok = mbar_wait(bars.ofull, (n_tiles - 1) & 1, abort_flag, a.status, kStatusTimeoutSoftmax);
+      if (ok) ok = mbar_wait(bars.xfull, 0, abort_flag, a.status, kStatusTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
@@ -383,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < D / 32; ++c) {
         float ov[32], xv[32];
         tmem_ld32(t_o + c * 32 + lane_base, ov);
-        tmem_ld32(t_x + c * 32 + lane_base, xv);
+        tmem_ld32(t_s2 + c * 32 + lane_base, xv);
         tmem_wait_ld();
         uint32_t w[16];
 #pragma unroll
@@ -420,28 +582,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+template <int D, bool FOLD>
+int launch_coarse_t(const CoarseLaunch& L, cudaStream_t s) {
+  const CoarseArgs& a = L.args;
+  dim3 grid(a.rows / 128, a.banks);
+  int smem = CoarseSmem<D, FOLD>::kTotal + 1024;
+  if (smem < 120 * 1024) smem = 120 * 1024;  // one CTA per SM: it holds all 512 TMEM columns
+  cudaFuncSetAttribute(coarse_kernel<D, FOLD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  coarse_kernel<D, FOLD><<<grid, kThreads, smem, s>>>(L.tm_q, L.tm_basis_t, L.tm_cvk, L.tm_kmean, L.tm_var,
+                                                      L.tm_vmean_t, a);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
 }  // namespace
 
 int launch_coarse(const CoarseLaunch& L, cudaStream_t s) {
   const CoarseArgs& a = L.args;
-  if (a.rows % 128 || a.nB_pad % 128 || a.nB_pad > kMaxBlocks) return kErrShape;
+  if (a.rows % 128 || a.nB_pad % kTileN || a.nB_pad > kMaxBlocks || a.rank < 0) return kErrShape;
   if (a.rows == 0) return kOk;
-  dim3 grid(a.rows / 128, a.banks);
-  if (L.D == 128) {
-    const int smem = CoarseSmem<128>::kTotal + 1024;
-    cudaFuncSetAttribute(coarse_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    coarse_kernel<128><<<grid, kThreads, smem, s>>>(L.tm_q, L.tm_basis_t, L.tm_cvk, L.tm_kmean, L.tm_var,
-                                                    L.tm_vmean_t, a);
-  } else if (L.D == 64) {
-    int smem = CoarseSmem<64>::kTotal + 1024;
-    if (smem < 120 * 1024) smem = 120 * 1024;  // one CTA per SM: it holds all 512 TMEM columns
-    cudaFuncSetAttribute(coarse_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    coarse_kernel<64><<<grid, kThreads, smem, s>>>(L.tm_q, L.tm_basis_t, L.tm_cvk, L.tm_kmean, L.tm_var,
-                                                   L.tm_vmean_t, a);
-  } else {
-    return kErrShape;
-  }
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+  const bool fold = a.rank > 0 && a.rank + 2 <= 64 && a.rank + 2 <= L.D;
+  if (L.D == 128) return fold ? launch_coarse_t<128, true>(L, s) : launch_coarse_t<128, false>(L, s);
+  if (L.D == 64) return fold ? launch_coarse_t<64, true>(L, s) : launch_coarse_t<64, false>(L, s);
+  return kErrShape;
 }
 
 }  // namespace recap

@@ -111,6 +111,7 @@ int launch_basis_prep(const BasisPrepArgs& a, cudaStream_t s);
 struct CoarseArgs {
   int banks, S_pad, D, nB, nB_pad, rows, n_video;
   float scale, theta;
+  int rank;                      // w is folded at this rank (columns >= rank equal); 0: not folded
   const uint8_t* partition;      // [banks, nB, nB]
   const float* counts_log;       // [nB] ln(tokens per video block)
   const float* old_lse;          // [banks, rows] coarse LSE at the last refresh (nullable)

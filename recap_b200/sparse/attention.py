@@ -333,7 +333,8 @@ class SparseAttention:
             _lib.ptr(inputs.k_mean_bf16), _lib.ptr(context["variance_bf16"]), _lib.ptr(inputs.v_mean_t_bf16),
             _lib.ptr(partition), _lib.ptr(counts_log(self.geometry, dev)), _lib.ptr(old_lse),
             sh.banks, sh.S, sh.D, sh.n_video, float(scale), float(self.config.closure_gate_theta),
-            _lib.ptr(out), _lib.ptr(lse), _lib.ptr(partial), _lib.ptr(center), _lib.ptr(status),
+            int(self.config.closure_rank), _lib.ptr(out), _lib.ptr(lse), _lib.ptr(partial), _lib.ptr(center),
+            _lib.ptr(status),
             _lib.stream_handle(dev),
         )
         return out, lse, center

@@ -37,12 +37,13 @@ def _strided_qkv(b, h, s, d, seed):
     return out
 
 
-def _run_gather(layout, q, k, v, q_mean=True):
+def _run_gather(layout, q, k, v, q_mean=True, closure_rank=None):
     from recap_b200.config import OperatorConfig
     from recap_b200.sparse.attention import SparseAttention, SparseGeometry
 
     geo = SparseGeometry.build(layout, 128)
-    sa = SparseAttention(geo, OperatorConfig())
+    cfg = OperatorConfig() if closure_rank is None else OperatorConfig(closure_rank=closure_rank)
+    sa = SparseAttention(geo, cfg)
     return sa, sa.prepare(q, k, v, q_mean=q_mean)
 
 
@@ -293,9 +294,21 @@ def test_closure_statistics_vs_oracle(d, nv, text, text_first):
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("nv,text,text_first", [(2048, 0, False), (700, 50, True)])
 def test_coarse_tail_vs_oracle(d, nv, text, text_first):
+    _check_coarse_tail(d, nv, text, text_first, None)
+
+
+@pytest.mark.parametrize("d,rank", [(128, 0), (64, 0), (128, 20), (64, 62), (128, 1)])
+def test_coarse_tail_ranks_vs_oracle(d, rank):
+    """The quadratic term over a folded variance (rank + 2 columns, one to four K-steps)
+    and over the full head dimension (rank 0: not folded), with 291 key blocks: three
+    tiles of block means through the operand rings, the last one mostly padding."""
+    _check_coarse_tail(d, 128 * 290 + 77, 50, True, rank)
+
+
+def _check_coarse_tail(d, nv, text, text_first, rank):
     lay = _layout(nv, text, text_first)
     q, k, v = _strided_qkv(1, 2, nv + text, d, seed=8)
-    sa, inp = _run_gather(lay, q, k, v, q_mean=True)
+    sa, inp = _run_gather(lay, q, k, v, q_mean=True, closure_rank=rank)
     sh = inp.shapes
     scale = 1 / math.sqrt(d)
     part = sa.head_partition(inp, scale)
