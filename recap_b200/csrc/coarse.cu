@@ -22,12 +22,16 @@
 //
 // The omitted set is a mask over all nB block means, processed in tiles of 128
 // (kbar, w and vbar^T of a bank stay in L2).  One CTA per (query block, bank),
-// 8 warps:
+// 12 warps:
 //   warp 0      TMA producer of Q, U^T (prologue), the (kbar, w) tiles and C_vk;
 //   warp 1      TMEM allocator and MMA issuer;
 //   warp 2      TMA producer of the vbar^T tiles;
-//   warps 4-7   one query row per thread: qsq, the gated online softmax (log2
-//               domain, lazy rescaling of O), P into TMEM, the epilogue.
+//   warps 4-11  two threads per query row (warps w and w + 4 share TMEM lanes), each
+//               with half of every tile's 64-block halves and half of the head
+//               dimension: qsq, the gated online softmax (log2 domain, lazy rescaling
+//               of O, the row maximum exchanged between the halves every tile), P
+//               into TMEM, the epilogue.  Two softmax warps per SM sub-partition hide
+//               each other's latencies.
 // TMEM: S1 = Q kbar^T double-buffered in columns [0,128) and [128,256), S2 = qsq w^T
 // in [256,384), O in [384,384+D).  Q U goes to the O columns before the first P.V,
 // and the drift Q C_vk^T to the S2 columns after the last S2 has been read.  P
@@ -43,7 +47,7 @@
 namespace recap {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
 constexpr int kSoftmaxWarp0 = 4;
 constexpr int kTileN = 128;         // block means per tile
 constexpr int kMaxBlocks = 2048;    // nB_pad limit (column terms in shared memory)
@@ -67,10 +71,12 @@ struct CoarseSmem {
   static constexpr int kKWRing = kQsq + kQsqBytes;
   static constexpr int kVRing = kKWRing + kKWStages * kKW;
   static constexpr int kCol = kVRing + kVStages * kOpV;       // fp32 column terms [kMaxBlocks]
-  static constexpr int kBars = kCol + kMaxBlocks * 4;
+  static constexpr int kXchg = kCol + kMaxBlocks * 4;  // row maxima [2 parity][2 halves][128]
+  static constexpr int kSums = kXchg + 2 * 2 * 128 * 4;  // (l, g) per half [2][2][128], then T partials [128]
+  static constexpr int kBars = kSums + (2 * 2 * 128 + 128) * 4;
   // pro_full, pro_mma, qsq_ready, kw_full[2], kw_empty[2], v_full[2], v_empty[2],
-  // s1full[2], s2full, s2free, pfull, ofull, c_full, xfull, done
-  static constexpr int kNumBars = 3 + 8 + 2 + 8;
+  // s1full[2], s2full, s2free, pfull, ofull, c_full, xfull, done, xchg[2], xsum, tpart
+  static constexpr int kNumBars = 3 + 8 + 2 + 7 + 4;
   static constexpr int kMisc = kBars + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16 + 4 * 4;
   static_assert(kOpV >= D * D * 2, "U^T is staged in a vbar^T slot");
@@ -79,7 +85,7 @@ struct CoarseSmem {
 
 struct CoarseBars {
   uint64_t *pro_full, *pro_mma, *qsq_ready, *kw_full, *kw_empty, *v_full, *v_empty, *s1full, *s2full, *s2free,
-      *pfull, *ofull, *c_full, *xfull, *done;
+      *pfull, *ofull, *c_full, *xfull, *done, *xchg, *xsum, *tpart;
 };
 
 __device__ __forceinline__ CoarseBars carve(uint8_t* base) {
@@ -100,6 +106,9 @@ __device__ __forceinline__ CoarseBars carve(uint8_t* base) {
   r.c_full = b + 17;
   r.xfull = b + 18;
   r.done = b + 19;
+  r.xchg = b + 20;  // [2]
+  r.xsum = b + 22;
+  r.tpart = b + 23;
   return r;
 }
 
@@ -120,6 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sKW = smem + L::kKWRing;
   uint8_t* sV = smem + L::kVRing;
   float* colterm = reinterpret_cast<float*>(smem + L::kCol);
+  float* rowmax = reinterpret_cast<float*>(smem + L::kXchg);
+  float* rowsums = reinterpret_cast<float*>(smem + L::kSums);
   CoarseBars bars = carve(smem + L::kBars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
@@ -137,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(bars.pro_full, 1);
     mbar_init(bars.pro_mma, 1);
-    mbar_init(bars.qsq_ready, 4);
+    mbar_init(bars.qsq_ready, 8);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bars.kw_full + s, 1);
       mbar_init(bars.kw_empty + s, 1);
@@ -146,8 +157,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bars.s1full + s, 1);
     }
     mbar_init(bars.s2full, 1);
-    mbar_init(bars.s2free, 4);
-    mbar_init(bars.pfull, 4);
+    mbar_init(bars.s2free, 8);
+    mbar_init(bars.pfull, 8);
+    mbar_init(bars.xchg, 8);
+    mbar_init(bars.xchg + 1, 8);
+    mbar_init(bars.xsum, 8);
+    mbar_init(bars.tpart, 4);
     mbar_init(bars.ofull, 1);
     mbar_init(bars.c_full, 1);
     mbar_init(bars.xfull, 1);
@@ -350,60 +365,80 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kSoftmaxWarp0) {
     // ================================================================ softmax + epilogue
-    const int t = threadIdx.x - kSoftmaxWarp0 * 32;
-    const int q4 = warp - kSoftmaxWarp0;
+    const int h = (warp - kSoftmaxWarp0) >> 2;  // half: blocks [64h, 64h + 64) of each tile
+    const int q4 = warp & 3;                    // TMEM lane quarter this warp may access
+    const int t = q4 * 32 + lane;               // query row
     const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
+    constexpr int kHalf = kTileN / 2;           // block means per thread and tile
+    constexpr int kDh = D / 2;                  // head-dimension columns per thread
     const float scale = a.scale;
-    const float s_l2 = scale * kLog2e;                      // S1 -> log2 units
-    const float h_l2 = 0.5f * scale * scale * kLog2e;       // gated S2 -> log2 units
+    const float s_l2 = scale * kLog2e;                           // S1 -> log2 units
+    const float h_l2 = 0.5f * scale * scale * kLog2e;            // gated S2 -> log2 units
     const float gate_max = a.theta * a.theta / (scale * scale);  // s^2 quad <= theta^2
-    bool ok = mbar_wait(bars.pro_mma, 0, abort_flag, a.status, kStatusTimeoutSoftmax);
-    ok = __all_sync(0xffffffffu, ok);
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+      bool r = mbar_wait(bar, parity, abort_flag, a.status, kStatusTimeoutSoftmax);
+      return __all_sync(0xffffffffu, r);
+    };
+    bool ok = wait_all(bars.pro_mma, 0);
     if (ok) {
       tc_fence_after();
       // qsq = bf16(bf16(q U)^2): the A operand of the quadratic term (row t, K-major,
-      // 128-byte swizzle)
+      // 128-byte swizzle); each half squares D/2 columns of q U
       const uint32_t qsq_row = smem_u32(sQsq) + t * 128;
       if (FOLD) {
-        // zero the row's 16 k2 columns, then (qsq_0 .. qsq_{rank-1}, T_hi, T_lo)
+        // (qsq_0 .. qsq_{rank-1}, T_hi, T_lo, 0 ...) over 16 k2 columns: each half stores
+        // the qsq_k of its own columns, half 0 the rest
         const int rank = a.rank;
-        for (int k = 0; k < 16 * k2; k += 8)
-          st_shared_v4(qsq_row + (((k >> 3) ^ (t & 7)) << 4), 0u, 0u, 0u, 0u);
         float tail = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < kDh / 32; ++c) {
           float v[32];
-          tmem_ld32(t_o + c * 32 + lane_base, v);
+          tmem_ld32(t_o + h * kDh + c * 32 + lane_base, v);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const int k = c * 32 + e;
-            const float x = bf16_round(v[e]);
-            const float q2 = bf16_round(x * x);
+            const int k = h * kDh + c * 32 + e;
+            const float xq = bf16_round(v[e]);
+            const float q2 = bf16_round(xq * xq);
             if (k < rank) {
-              const __nv_bfloat16 h = __float2bfloat16_rn(q2);
+              const __nv_bfloat16 hb = __float2bfloat16_rn(q2);
               asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k >> 3) ^ (t & 7)) << 4) + (k & 7) * 2),
-                           "h"(*reinterpret_cast<const unsigned short*>(&h))
+                           "h"(*reinterpret_cast<const unsigned short*>(&hb))
                            : "memory");
             } else {
               tail += q2;
             }
           }
         }
-        const __nv_bfloat16 hi = __float2bfloat16_rn(tail);
-        const __nv_bfloat16 lo = __float2bfloat16_rn(tail - __bfloat162float(hi));
-        const int k_hi = rank, k_lo = rank + 1;
-        asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_hi >> 3) ^ (t & 7)) << 4) + (k_hi & 7) * 2),
-                     "h"(*reinterpret_cast<const unsigned short*>(&hi))
-                     : "memory");
-        asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_lo >> 3) ^ (t & 7)) << 4) + (k_lo & 7) * 2),
-                     "h"(*reinterpret_cast<const unsigned short*>(&lo))
-                     : "memory");
+        float* tp = rowsums + 2 * 2 * 128;  // past the (l, g) sums: T partials of half 1
+        if (h == 1) {
+          tp[t] = tail;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bars.tpart);
+        } else {
+          ok = wait_all(bars.tpart, 0);
+          if (ok) {
+            tail += tp[t];
+            const __nv_bfloat16 hi = __float2bfloat16_rn(tail);
+            const __nv_bfloat16 lo = __float2bfloat16_rn(tail - __bfloat162float(hi));
+            const int k_hi = rank, k_lo = rank + 1;
+            asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_hi >> 3) ^ (t & 7)) << 4) + (k_hi & 7) * 2),
+                         "h"(*reinterpret_cast<const unsigned short*>(&hi))
+                         : "memory");
+            asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_lo >> 3) ^ (t & 7)) << 4) + (k_lo & 7) * 2),
+                         "h"(*reinterpret_cast<const unsigned short*>(&lo))
+                         : "memory");
+            for (int k = rank + 2; k < 16 * k2; ++k)
+              asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k >> 3) ^ (t & 7)) << 4) + (k & 7) * 2),
+                           "h"(static_cast<unsigned short>(0))
+                           : "memory");
+          }
+        }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < kDh / 32; ++c) {
           float v[32];
-          tmem_ld32(t_o + c * 32 + lane_base, v);
+          tmem_ld32(t_o + h * kDh + c * 32 + lane_base, v);
           tmem_wait_ld();
           uint32_t pk[16];
 #pragma unroll
@@ -414,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const int k = c * 32 + q * 8;
+            const int k = h * kDh + c * 32 + q * 8;
             st_shared_v4(qsq_row + (k >> 6) * 16384 + ((((k & 63) >> 3) ^ (t & 7)) << 4), pk[4 * q], pk[4 * q + 1],
                          pk[4 * q + 2], pk[4 * q + 3]);
           }
@@ -425,36 +460,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bars.qsq_ready);
     }
-    float m_run = -INFINITY;  // running max (log2 domain)
-    float l_run = 0.f, g_run = 0.f;
+    float m_run = -INFINITY;  // running max (log2 domain), identical in both halves
+    float l_run = 0.f, g_run = 0.f;  // this half's share of the row sum and of the gated mass
     for (int j = 0; ok && j < n_tiles; ++j) {
       const int b = j & 1;
-      ok = mbar_wait(bars.s1full + b, (j >> 1) & 1, abort_flag, a.status, kStatusTimeoutSoftmax);
-      if (ok) ok = mbar_wait(bars.s2full, j & 1, abort_flag, a.status, kStatusTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = wait_all(bars.s1full + b, (j >> 1) & 1);
+      if (ok) ok = wait_all(bars.s2full, j & 1);
       if (!ok) break;
       tc_fence_after();
-      float x[kTileN];
-      uint32_t gate[4];
+      float x[kHalf];
+      uint32_t gate[2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float v1[32], v2[32];
-        tmem_ld32(t_s1 + b * kTileN + c * 32 + lane_base, v1);
-        tmem_ld32(t_s2 + c * 32 + lane_base, v2);
+        tmem_ld32(t_s1 + b * kTileN + h * kHalf + c * 32 + lane_base, v1);
+        tmem_ld32(t_s2 + h * kHalf + c * 32 + lane_base, v2);
         tmem_wait_ld();
-        const float4* ct4 = reinterpret_cast<const float4*>(colterm + j * kTileN + c * 32);
+        const float4* ct4 = reinterpret_cast<const float4*>(colterm + j * kTileN + h * kHalf + c * 32);
         uint32_t gm = 0;
 #pragma unroll
         for (int e4 = 0; e4 < 8; ++e4) {
           const float4 ct = ct4[e4];
           const float cts[4] = {ct.x, ct.y, ct.z, ct.w};
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const int e = 4 * e4 + h;
+          for (int i = 0; i < 4; ++i) {
+            const int e = 4 * e4 + i;
             const float quad = v2[e];
             const bool gt = quad <= gate_max;
             gm |= gt ? (1u << e) : 0u;
-            x[c * 32 + e] = fmaf(quad, gt ? h_l2 : 0.f, fmaf(v1[e], s_l2, cts[h]));
+            x[c * 32 + e] = fmaf(quad, gt ? h_l2 : 0.f, fmaf(v1[e], s_l2, cts[i]));
           }
         }
         // opaque copy: the exponential phase then tests these packed bits instead of the
@@ -469,11 +503,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx[k] = max3(x[k], x[8 + k], x[16 + k]);
 #pragma unroll
-      for (int i = 24; i < kTileN; i += 16) {
+      for (int i = 24; i < kHalf - 8; i += 16) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], x[i + k], x[i + 8 + k]);
       }
-      const float m_tile = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], x[kHalf - 8 + k]);
+      float m_half = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+      // exchange the half maxima (double-buffered by tile parity); this also orders the
+      // other half's S1 reads before this half's P stores into the S1 columns
+      rowmax[(b * 2 + h) * 128 + t] = m_half;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars.xchg + b);
+      ok = wait_all(bars.xchg + b, (j >> 1) & 1);
+      if (!ok) break;
+      const float m_tile = fmaxf(m_half, rowmax[(b * 2 + (h ^ 1)) * 128 + t]);
       float alpha = 1.f;
       bool rescale = false;
       if (m_tile != -INFINITY) {
@@ -487,37 +531,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // O must hold P.V(j-1) before it is rescaled; P.V(j) starts after pfull below
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-        ok = mbar_wait(bars.ofull, (j - 1) & 1, abort_flag, a.status, kStatusTimeoutSoftmax);
-        ok = __all_sync(0xffffffffu, ok);
+        ok = wait_all(bars.ofull, (j - 1) & 1);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < D / 8; ++c) {
+        for (int c = 0; c < kDh / 8; ++c) {
           float o[8];
-          tmem_ld8(t_o + c * 8 + lane_base, o);
+          tmem_ld8(t_o + h * kDh + c * 8 + lane_base, o);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 8; i += 2) mul2(o[i], o[i + 1], alpha, alpha);
-          tmem_st8(t_o + c * 8 + lane_base, o);
+          tmem_st8(t_o + h * kDh + c * 8 + lane_base, o);
         }
       }
       const float neg_m = m_run == -INFINITY ? 0.f : -m_run;  // exp2(-inf + 0) = 0
       float ls[4] = {0.f, 0.f, 0.f, 0.f}, gs[2] = {0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int e0 = 2 * i, e1 = 2 * i + 1;
-          const float p0 = fast_exp2(x[c * 32 + e0] + neg_m);
-          const float p1 = fast_exp2(x[c * 32 + e1] + neg_m);
+          float y0 = x[c * 32 + e0], y1 = x[c * 32 + e1];
+          add2(y0, y1, neg_m, neg_m);
+          const float p0 = fast_exp2(y0);
+          const float p1 = fast_exp2(y1);
           add2(ls[(i & 1) * 2], ls[(i & 1) * 2 + 1], p0, p1);
           const float g0 = ((gate[c] >> e0) & 1u) ? p0 : 0.f;
           const float g1 = ((gate[c] >> e1) & 1u) ? p1 : 0.f;
           add2(gs[0], gs[1], g0, g1);
           pk[i] = pack_bf16(p0, p1);
         }
-        tmem_st16(t_s1 + b * kTileN + c * 16 + lane_base, pk);
+        // P of blocks 64h + 32c .. + 31 (two per column)
+        tmem_st16(t_s1 + b * kTileN + h * (kHalf / 2) + c * 16 + lane_base, pk);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -526,36 +572,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       l_run = l_run * alpha + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
       g_run = g_run * alpha + (gs[0] + gs[1]);
     }
+    // combine the halves' row sums
+    float l_tot = l_run, g_tot = g_run;
     if (ok) {
-      ok = mbar_wait(bars.ofull, (n_tiles - 1) & 1, abort_flag, a.status, kStatusTimeoutSoftmax);
-      if (ok) ok = mbar_wait(bars.xfull, 0, abort_flag, a.status, kStatusTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
+      rowsums[(h * 2 + 0) * 128 + t] = l_run;
+      rowsums[(h * 2 + 1) * 128 + t] = g_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars.xsum);
+      ok = wait_all(bars.xsum, 0);
+      if (ok) {
+        l_tot += rowsums[((h ^ 1) * 2 + 0) * 128 + t];
+        g_tot += rowsums[((h ^ 1) * 2 + 1) * 128 + t];
+      }
+    }
+    if (ok) {
+      ok = wait_all(bars.ofull, (n_tiles - 1) & 1);
+      if (ok) ok = wait_all(bars.xfull, 0);
     }
     if (ok) {
       tc_fence_after();
-      const bool has_tail = l_run > 0.f;
-      const float safe_l = fmaxf(l_run, 1.0e-30f);
+      const bool has_tail = l_tot > 0.f;
+      const float safe_l = fmaxf(l_tot, 1.0e-30f);
       const float inv_l = 1.f / safe_l;
-      const float lse = has_tail ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
-      const float g_bf = bf16_round(has_tail ? g_run * inv_l : 0.f);
+      const float lse = has_tail ? (m_run + __log2f(l_tot)) * 0.69314718055994531f : -INFINITY;
+      const float g_bf = bf16_round(has_tail ? g_tot * inv_l : 0.f);
       const int r = qb * 128 + t;
       const size_t orow = static_cast<size_t>(bank) * a.rows + r;
-      __nv_bfloat16* dst = a.out + orow * D;
+      __nv_bfloat16* dst = a.out + orow * D + h * kDh;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < kDh / 32; ++c) {
         float ov[32], xv[32];
-        tmem_ld32(t_o + c * 32 + lane_base, ov);
-        tmem_ld32(t_s2 + c * 32 + lane_base, xv);
+        tmem_ld32(t_o + h * kDh + c * 32 + lane_base, ov);
+        tmem_ld32(t_s2 + h * kDh + c * 32 + lane_base, xv);
         tmem_wait_ld();
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           float res[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float o = has_tail ? bf16_round(ov[2 * e + h] * inv_l) : 0.f;
-            const float drift = bf16_round(scale * bf16_round(xv[2 * e + h]));
-            res[h] = o + bf16_round(g_bf * drift);
+          for (int i = 0; i < 2; ++i) {
+            const float o = has_tail ? bf16_round(ov[2 * e + i] * inv_l) : 0.f;
+            const float drift = bf16_round(scale * bf16_round(xv[2 * e + i]));
+            res[i] = o + bf16_round(g_bf * drift);
           }
           w[e] = pack_bf16(res[0], res[1]);
         }
@@ -563,11 +621,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q) st_stream_v4(d4 + q, make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]));
       }
-      a.lse[orow] = lse;
-      if (a.center_partial != nullptr) {
-        float dv = lse - a.old_lse[orow];
-        for (int o = 16; o > 0; o >>= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
-        if (lane == 0) row_part[q4] = dv;
+      if (h == 0) {
+        a.lse[orow] = lse;
+        if (a.center_partial != nullptr) {
+          float dv = lse - a.old_lse[orow];
+          for (int o = 16; o > 0; o >>= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
+          if (lane == 0) row_part[q4] = dv;
+        }
       }
     }
   }
