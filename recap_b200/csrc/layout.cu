@@ -16,6 +16,7 @@
 //    orthonormal U equals (trace of the block covariance - the leading variances) /
 //    (D - rank), so only K U[:, :rank] is formed.
 // Rows past S (up to S_pad) are written as zeros.  HBM-bound.
+#include "common.cuh"
 #include "kernels.h"
 
 namespace recap {
@@ -47,7 +48,7 @@ struct GatherSmem {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a) {
   using L = GatherSmem<D>;
   constexpr int CPR = D / 8;              // 16-byte chunks per row
   constexpr int RPP = kThreads / CPR;     // rows per pass
@@ -72,23 +73,38 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
   const int video_rows = min(128, a.n_video - row0);  // <= 0 for text-only blocks
   const bool need_k_tile = (a.kct != nullptr || a.variance != nullptr) && video_rows > 0;
 
-  for (int t = 0; t < 3; ++t) {
+  // Native rows of this thread's PASSES rows, then each tensor's PASSES row chunks in
+  // one burst of independent loads (two tensors in flight): the pass is bound by the
+  // latency of these gathers.
+  int nat[PASSES];
+#pragma unroll
+  for (int p = 0; p < PASSES; ++p) {
+    const int r = row0 + p * RPP + rsub;
+    int n = -1;
+    if (r < a.S) {
+      n = a.src_row[r];
+      if (n < 0 || n >= a.S) n = -1;  // a corrupt index reads nothing out of bounds
+    }
+    nat[p] = n;
+  }
+  auto load_rows = [&](int t, uint4 (&v)[PASSES]) {
     const __nv_bfloat16* src = a.src[t];
-    if (src == nullptr) continue;
-    const __nv_bfloat16* base = src + bi * a.stride_b[t] + hi * a.stride_h[t];
+    if (src == nullptr) return;
+    const __nv_bfloat16* base = src + bi * a.stride_b[t] + hi * a.stride_h[t] + ch * 8;
+#pragma unroll
+    for (int p = 0; p < PASSES; ++p)
+      v[p] = nat[p] >= 0 ? ld_stream_v4(base + static_cast<int64_t>(nat[p]) * a.stride_s[t]) : make_uint4(0, 0, 0, 0);
+  };
+  auto process = [&](int t, const uint4 (&v)[PASSES]) {
+    if (a.src[t] == nullptr) return;
     float acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-#pragma unroll 4
+#pragma unroll
     for (int p = 0; p < PASSES; ++p) {
       const int rl = p * RPP + rsub;
       const int r = row0 + rl;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      if (r < a.S) {
-        const int64_t native = a.src_row[r];
-        if (native >= 0 && native < a.S)  // a corrupt index reads nothing out of bounds
-          val = *reinterpret_cast<const uint4*>(base + native * a.stride_s[t] + ch * 8);
-      }
+      const uint4 val = v[p];
       if (t == 0 && a.qr) {
         *reinterpret_cast<uint4*>(a.qr + (static_cast<size_t>(bank) * a.S_pad + r) * D + ch * 8) = val;
       } else if (t == 1) {
@@ -106,10 +122,10 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
       for (int e = 0; e < 8; ++e) red[rsub * D + ch * 8 + e] = acc[e];
       __syncthreads();
       if (tid < D) {
-        float s = 0.f;
+        float sum = 0.f;
 #pragma unroll 4
-        for (int g = 0; g < RPP; ++g) s += red[g * D + tid];
-        const float m = s / static_cast<float>(video_rows);
+        for (int g = 0; g < RPP; ++g) sum += red[g * D + tid];
+        const float m = sum / static_cast<float>(video_rows);
         if (t == 1) kmean_s[tid] = m;
         if (a.mean[t]) a.mean[t][(static_cast<size_t>(bank) * a.nB + blk) * D + tid] = m;
         if (t == 1 && a.kmean_bf16)
@@ -119,6 +135,15 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a) {
       }
       __syncthreads();
     }
+  };
+  {
+    uint4 va[PASSES], vb[PASSES];
+    load_rows(0, va);
+    load_rows(1, vb);
+    process(0, va);
+    load_rows(2, va);
+    process(1, vb);
+    process(2, va);
   }
 
   __syncthreads();  // the staged V and K tiles are complete before anyone reads them back
