@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define RECAP_B200_ABI_VERSION 4
+#define RECAP_B200_ABI_VERSION 5
 
 #define RECAP_OK 0
 #define RECAP_ERR_SHAPE 1
@@ -42,6 +42,7 @@ extern "C" {
 #define RECAP_STATUS_TIMEOUT_MMA 102
 #define RECAP_STATUS_TIMEOUT_SOFTMAX 103
 #define RECAP_STATUS_TIMEOUT_PRODUCER 104
+#define RECAP_STATUS_TIMEOUT_SELFTEST 106 /* recap_wait_selftest only */
 
 int recap_abi_version(void);
 
@@ -207,6 +208,15 @@ int recap_refresh_detail_noalloc(const void* full_o, const float* full_lse, cons
  * counterpart in the reference; tests compare it with the CUDA exp2f of the same
  * inputs. */
 int recap_exp2_check(const float* in, float* out, int n, void* stream);
+
+/* Self-check of the bounded waits that every kernel of this library uses on its
+ * on-chip barriers (no counterpart in the reference).  One thread waits on an
+ * mbarrier that nothing arrives on until limit_ns (at most 1 s) runs out, writes
+ * RECAP_STATUS_TIMEOUT_SELFTEST to *status and raises the block's abort flag; a second
+ * waiter with a 4x longer limit leaves through that flag.  result[0], result[1]: 1 if
+ * the first / second wait completed (expected 0); result[2]: the second waiter's time
+ * in ns (about limit_ns, not 4x).  Nothing faults or hangs; the context stays usable. */
+int recap_wait_selftest(int* status, long long limit_ns, long long* result, void* stream);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,7 @@ import torch
 PACKAGE_DIR = Path(__file__).resolve().parent
 LIB_PATH = PACKAGE_DIR / "librecap_b200.so"
 
-ABI_VERSION = 4  # RECAP_B200_ABI_VERSION of include/recap_b200.h
+ABI_VERSION = 5  # RECAP_B200_ABI_VERSION of include/recap_b200.h
 
 RECAP_OK = 0
 RECAP_ERR_SHAPE = 1
@@ -30,6 +30,7 @@ STATUS_NAMES = {
     102: "MMA wait timed out",
     103: "softmax wait timed out",
     104: "producer wait timed out",
+    106: "self-test wait timed out (expected from recap_wait_selftest)",
 }
 
 _P = ctypes.c_void_p
@@ -59,6 +60,7 @@ SIGNATURES: dict[str, tuple] = {
     "recap_refresh_detail": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
     "recap_refresh_detail_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
     "recap_exp2_check": (_I, [_P, _P, _I, _P]),
+    "recap_wait_selftest": (_I, [_P, _I64, _P, _P]),
 }
 
 _lib = None

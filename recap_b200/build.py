@@ -20,7 +20,8 @@ LIB_NAME = "librecap_b200.so"
 LIB_PATH = PACKAGE_DIR / LIB_NAME
 BUILD_DIR = PACKAGE_DIR / "_build"
 
-SOURCES = ["layout.cu", "select.cu", "closure.cu", "cvk.cu", "coarse.cu", "fmha.cu", "refresh.cu", "capi.cu"]
+SOURCES = ["layout.cu", "select.cu", "closure.cu", "cvk.cu", "coarse.cu", "fmha.cu", "refresh.cu", "selftest.cu",
+           "capi.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",

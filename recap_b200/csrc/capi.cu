@@ -336,6 +336,10 @@ int recap_exp2_check(const float* in, float* out, int n, void* stream) {
   return launch_exp2_check(in, out, n, static_cast<cudaStream_t>(stream));
 }
 
+int recap_wait_selftest(int* status, long long limit_ns, long long* result, void* stream) {
+  return launch_wait_selftest(status, limit_ns, result, static_cast<cudaStream_t>(stream));
+}
+
 int recap_refresh_partials(int banks, int n_video) {
   return refresh_partials_count(banks, (n_video / 128) * 128);
 }

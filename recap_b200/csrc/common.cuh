@@ -25,6 +25,7 @@ enum : int {
   kStatusTimeoutSoftmax = 103,
   kStatusTimeoutProducer = 104,
   kStatusBadList = 105,
+  kStatusTimeoutSelftest = 106,
 };
 
 // Longest a single mbarrier wait may last before the kernel gives up (ns of
@@ -78,11 +79,12 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Wait for the phase with the given parity to complete.  Returns false when the
-// wait ran out of time or another role of the CTA aborted; in both cases the
-// CTA-local abort flag is set and (on timeout) the status word records `code`.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
+// Wait for the phase with the given parity to complete, for at most limit_ns.
+// Returns false when the wait ran out of time or another role of the CTA aborted;
+// in both cases the CTA-local abort flag is set and (on timeout) the status word
+// records `code`.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                             int* status, int code, uint64_t limit_ns) {
   uint64_t start = 0;
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -91,13 +93,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       const uint64_t now = global_ns();
       if (start == 0) {
         start = now;
-      } else if (now - start > kWaitNs) {
+      } else if (now - start > limit_ns) {
         *abort_flag = 1;
         if (status) atomicCAS(status, 0, code);
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int code) {
+  return mbar_wait_ns(bar, parity, abort_flag, status, code, kWaitNs);
 }
 
 // Bounded wait used on the way out (draining copies or MMAs in flight): gives up

@@ -539,26 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-__global__ void exp2_check_kernel(const float* in, float* out, int n) {
-  const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
-  if (i >= n) return;
-  const float y0 = in[i];
-  const float y1 = i + 1 < n ? in[i + 1] : 0.f;
-  float p0, p1;
-  exp2_poly2(p0, p1, y0, y1);
-  out[i] = p0;
-  if (i + 1 < n) out[i + 1] = p1;
-}
-
 }  // namespace
-
-int launch_exp2_check(const float* in, float* out, int n, cudaStream_t stream) {
-  if (n <= 0) return n == 0 ? kOk : kErrShape;
-  if (in == nullptr || out == nullptr) return kErrShape;
-  const int pairs = (n + 1) / 2;
-  exp2_check_kernel<<<(pairs + 255) / 256, 256, 0, stream>>>(in, out, n);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
-}
 
 int launch_fmha(const FmhaLaunch& L, cudaStream_t stream) {
   const FmhaArgs& a = L.args;

@@ -160,6 +160,8 @@ struct FmhaLaunch {
 int launch_fmha(const FmhaLaunch& L, cudaStream_t s);
 // out[i] = exp2_poly2(in[i]) (the softmax's FP32-pipe exponential)
 int launch_exp2_check(const float* in, float* out, int n, cudaStream_t s);
+// one bounded mbarrier wait that runs out (status word, abort flag); see selftest.cu
+int launch_wait_selftest(int* status, long long limit_ns, long long* result, cudaStream_t s);
 
 // ------------------------------------------------------------------ refresh
 struct RefreshArgs {

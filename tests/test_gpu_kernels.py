@@ -230,6 +230,36 @@ def test_exp2_poly_vs_exp2f():
     assert bool((out_low >= 0).all()) and float(out_low.max()) <= 2.0 ** -124
 
 
+def test_bounded_wait_runs_out_without_fault():
+    """The bounded mbarrier wait of every kernel, driven to its limit on purpose: a
+    barrier nothing arrives on.  The waiter records the timeout in the status word and
+    raises the block's abort flag; the second waiter leaves through the flag long before
+    its own (4x) limit; the context stays usable and the operator's status check raises."""
+    from recap_b200 import Operator, OperatorConfig, _lib as lib
+    from recap_b200.sparse import Layout, SparseGeometry
+
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    result = torch.full((3,), -1, dtype=torch.int64, device=DEV)
+    limit_ns = 50_000_000
+    lib.call("recap_wait_selftest", lib.ptr(status), limit_ns, lib.ptr(result), lib.stream_handle(torch.device(DEV)))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 106
+    r = result.cpu().tolist()
+    assert r[0] == 0 and r[1] == 0, r
+    assert limit_ns * 0.9 <= r[2] < 3 * limit_ns, r
+    # the context is still usable
+    x = torch.arange(1000, device=DEV, dtype=torch.float32)
+    assert float(x.sum()) == 499500.0
+    # the operator's status check reports a set status word, then clears it
+    lay = Layout.from_permutation(np.arange(1024), text_tokens=0, text_first=False)
+    op = Operator.build(OperatorConfig(), SparseGeometry.build(lay, 128), n_layers=1)
+    word = op.status_word(torch.device(DEV))
+    lib.call("recap_wait_selftest", lib.ptr(word), limit_ns, lib.ptr(result), lib.stream_handle(torch.device(DEV)))
+    with pytest.raises(RuntimeError, match="device timeout"):
+        op.check_device_status()
+    op.check_device_status()  # cleared
+
+
 def test_fmha_native_output_positions():
     nv, text, d = 700, 50, 64
     lay = _layout(nv, text, True)
