@@ -357,6 +357,8 @@ def run_ours(args) -> None:
     pk = peaks()
     achieved = flops / (fmha_ms * 1e-3) / 1e12 if fmha_ms else None
     traffic = traffic_per_launch()
+    if traffic is not None:
+        traffic = traffic * len(hs) / WORKLOAD["heads"]  # the committed figure is for all 24 heads on one GPU
 
     # end to end through the API with host buffers
     e2e = None
