@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define RECAP_B200_ABI_VERSION 5
+#define RECAP_B200_ABI_VERSION 6
 
 #define RECAP_OK 0
 #define RECAP_ERR_SHAPE 1
@@ -63,12 +63,18 @@ int recap_abi_version(void);
  *                  and 0 < rank < D, rank <= recap_gather_max_rank(), the per-block key
  *                  variances in U folded to `rank` (rotated_leaf_moments_triton + fold_rank,
  *                  recap/kernels/closure_stats.py:192-242, recap/sparse/closure.py:96-104):
- *                  variance [banks, nB, D] fp32, variance_bf16 [banks, nB_pad, D]. */
+ *                  variance [banks, nB, D] fp32, variance_bf16 [banks, nB_pad, D].
+ *   k_norm_max     [banks, NB] fp32 out (nullable): the largest |k| over the tokens of each
+ *                  128-token block (NB = ceil(S/128)); with it the attention kernels bound
+ *                  every logit q.k by |q| * k_norm_max and skip their running-max work.
+ *   k_mean_norm    [banks, nB] fp32 out (nullable): |bf16(kbar)| of each video block, the
+ *                  same bound for the coarse tail. */
 int recap_layout_gather(const void* q, const void* k, const void* v, const int64_t* strides, int batch,
                         int heads, int S, int D, int n_video, const int32_t* src_row, void* q_reordered,
                         void* k_reordered, void* v_transposed, float* q_mean, float* k_mean,
                         float* v_mean, void* k_mean_bf16, void* v_mean_t_bf16, void* k_centred_t,
-                        const float* basis, int rank, float* variance, void* variance_bf16, void* stream);
+                        const float* basis, int rank, float* variance, void* variance_bf16,
+                        float* k_norm_max, float* k_mean_norm, void* stream);
 
 /* Largest closure rank the layout pass folds itself (larger ranks: recap_closure_stats). */
 int recap_gather_max_rank(void);
@@ -150,11 +156,15 @@ int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const v
  * Replaces block_sparse_exact (recap/kernels/block_sparse.py:78-139) and, with
  * all_blocks = 1, the dense aten._scaled_dot_product_flash_attention of recap/operator.py:254-256.
  *   out            [banks, S, D] bf16; reordered row r is written at row out_pos[r]
- *                  (out_pos NULL: row r); lse [banks, S] fp32 likewise (nullable). */
+ *                  (out_pos NULL: row r); lse [banks, S] fp32 likewise (nullable).
+ *   k_norm_max     [banks, NB] from recap_layout_gather (nullable): with it, key blocks whose
+ *                  logit bound |q| * k_norm_max stays within 2^64 of a row's running maximum
+ *                  skip the per-block maximum and rescale (the same result up to fp32
+ *                  rounding); without it every block takes the exact path. */
 int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, const void* v_transposed,
-                            const uint8_t* partition, int banks, int S, int D, int n_video, int all_blocks,
-                            float scale, const int32_t* out_pos, void* out, float* lse, int* status,
-                            void* stream);
+                            const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
+                            int n_video, int all_blocks, float scale, const int32_t* out_pos, void* out,
+                            float* lse, int* status, void* stream);
 
 /* The corrected SPARSE step: block-sparse attention with the drift-weighted merge of the coarse
  * tail and the cached refinement fused as its epilogue, written in native order.
@@ -163,7 +173,8 @@ int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, co
  *   detail_value   [banks, rows, D] fp16, detail_log_mass/old_lse [banks, rows] fp32, center [banks]
  *   out            [banks, S, D] bf16, reordered row r at row out_pos[r]. */
 int recap_sparse_step(const void* q_reordered, const void* k_reordered, const void* v_transposed,
-                      const uint8_t* partition, int banks, int S, int D, int n_video, float scale,
+                      const uint8_t* partition, const float* k_norm_max, int banks, int S, int D, int n_video,
+                      float scale,
                       const void* coarse_out, const float* coarse_lse, const void* detail_value,
                       const float* detail_log_mass, const float* old_lse, const float* center,
                       const int32_t* out_pos, void* out, int* status, void* stream);

@@ -16,7 +16,7 @@ import torch
 PACKAGE_DIR = Path(__file__).resolve().parent
 LIB_PATH = PACKAGE_DIR / "librecap_b200.so"
 
-ABI_VERSION = 5  # RECAP_B200_ABI_VERSION of include/recap_b200.h
+ABI_VERSION = 6  # RECAP_B200_ABI_VERSION of include/recap_b200.h
 
 RECAP_OK = 0
 RECAP_ERR_SHAPE = 1
@@ -42,7 +42,7 @@ _F = ctypes.c_float
 SIGNATURES: dict[str, tuple] = {
     "recap_abi_version": (_I, []),
     "recap_layout_gather": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                 _P, _I, _P, _P, _P]),
+                                 _P, _I, _P, _P, _P, _P, _P]),
     "recap_gather_max_rank": (_I, []),
     "recap_cvk_workspace_floats": (_I64, [_I, _I, _I]),
     "recap_value_key_covariance": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
@@ -54,8 +54,8 @@ SIGNATURES: dict[str, tuple] = {
     "recap_basis_prep": (_I, [_P, _I, _I, _P, _P]),
     "recap_coarse_tail": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _I, _P, _P, _P, _P, _P,
                                _P]),
-    "recap_block_sparse_fmha": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P]),
-    "recap_sparse_step": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "recap_block_sparse_fmha": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P]),
+    "recap_sparse_step": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "recap_refresh_partials": (_I, [_I, _I]),
     "recap_refresh_detail": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
     "recap_refresh_detail_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),

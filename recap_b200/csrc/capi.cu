@@ -73,7 +73,8 @@ int recap_layout_gather(const void* q, const void* k, const void* v, const int64
                         int heads, int S, int D, int n_video, const int32_t* src_row, void* q_reordered,
                         void* k_reordered, void* v_transposed, float* q_mean, float* k_mean, float* v_mean,
                         void* k_mean_bf16, void* v_mean_t_bf16, void* k_centred_t, const float* basis, int rank,
-                        float* variance, void* variance_bf16, void* stream) {
+                        float* variance, void* variance_bf16, float* k_norm_max, float* k_mean_norm,
+                        void* stream) {
   Geom g;
   if (!geom(S, n_video, &g) || !d_ok(D) || batch <= 0 || heads <= 0 || strides == nullptr ||
       src_row == nullptr)
@@ -109,6 +110,8 @@ int recap_layout_gather(const void* q, const void* k, const void* v, const int64
   a.kct = static_cast<__nv_bfloat16*>(k_centred_t);
   a.basis = basis;
   a.rank = rank;
+  a.k_norm_max = k_norm_max;
+  a.k_mean_norm = k_mean_norm;
   a.variance = variance;
   a.variance_bf16 = static_cast<__nv_bfloat16*>(variance_bf16);
   if ((a.kct != nullptr || a.variance != nullptr) && k == nullptr) return kErrShape;
@@ -264,9 +267,9 @@ static int fmha_common(const void* q_reordered, const void* k_reordered, const v
 }
 
 int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, const void* v_transposed,
-                            const uint8_t* partition, int banks, int S, int D, int n_video, int all_blocks,
-                            float scale, const int32_t* out_pos, void* out, float* lse, int* status,
-                            void* stream) {
+                            const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
+                            int n_video, int all_blocks, float scale, const int32_t* out_pos, void* out,
+                            float* lse, int* status, void* stream) {
   Geom g;
   if (!geom(S, n_video, &g) || !d_ok(D) || banks <= 0 || out == nullptr) return kErrShape;
   if (!all_blocks && partition == nullptr) return kErrShape;
@@ -285,6 +288,7 @@ int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, co
   a.all_blocks = all_blocks;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.partition = partition;
+  a.k_norm_max = k_norm_max;
   a.epilogue = 0;
   a.out_pos = out_pos;
   a.o = static_cast<__nv_bfloat16*>(out);
@@ -294,7 +298,8 @@ int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, co
 }
 
 int recap_sparse_step(const void* q_reordered, const void* k_reordered, const void* v_transposed,
-                      const uint8_t* partition, int banks, int S, int D, int n_video, float scale,
+                      const uint8_t* partition, const float* k_norm_max, int banks, int S, int D, int n_video,
+                      float scale,
                       const void* coarse_out, const float* coarse_lse, const void* detail_value,
                       const float* detail_log_mass, const float* old_lse, const float* center,
                       const int32_t* out_pos, void* out, int* status, void* stream) {
@@ -318,6 +323,7 @@ int recap_sparse_step(const void* q_reordered, const void* k_reordered, const vo
   a.all_blocks = 0;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.partition = partition;
+  a.k_norm_max = k_norm_max;
   a.epilogue = 1;
   a.out_pos = out_pos;
   a.o = static_cast<__nv_bfloat16*>(out);

@@ -41,6 +41,9 @@ constexpr int kThreads = 320;
 constexpr int kSoftmaxWarp0 = 2;
 constexpr int kMaxKeyBlocks = 2048;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by 2^8
+// Largest logit excess over the running max (log2 units) the bounded path accepts: every
+// exponential stays below 2^64, finite in fp32 and bf16 with room for the row sums.
+constexpr float kBoundSlack = 64.0f;
 // Of the 16 column pairs of every 32-key chunk, the ones whose bit is set here take
 // their exponentials from exp2_poly2 on the FP32 pipe instead of the MUFU unit.  Off:
 // with one softmax warp per SM sub-partition and tile the extra FP32 instructions
@@ -370,8 +373,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale_log2 = args.scale_log2;
     float m_run = -INFINITY;  // running max, log2 domain (scaled)
     float l_run = 0.f;        // running row sum at m_run
+    // Logit bound: |q.k| <= |q| |k|, so every logit of key block j is at most
+    // qn_l2 * k_norm_max[j] (log2 units).  From the second block on, a warp whose rows all
+    // satisfy bound <= m_run + kBoundSlack exponentiates against m_run as it stands: no row
+    // maximum and no rescale, and every p stays below 2^kBoundSlack.  Other warps take the
+    // exact path.  The result is the same up to fp32 rounding; only the scale of the
+    // accumulated values differs, which the final division by the row sum removes.
+    float qn_l2 = INFINITY;
+    const float* knm = args.k_norm_max ? args.k_norm_max + static_cast<size_t>(it.bank) * NB : nullptr;
     bool ok = Lx > 0;
+    if (ok && knm != nullptr) {
+      // |q| of this row from the Q tile
+      ok = mbar_wait(bars.qfull, 0, abort_flag, args.status, kStatusTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      const uint32_t qrow = smem_u32(sQ) + x * kTileBytes + t * 128;
+      float ss = 0.f;
+#pragma unroll
+      for (int a = 0; a < D / 64; ++a) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t w0, w1, w2, w3;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                       : "r"(qrow + a * 16384 + ((c ^ (t & 7)) << 4)));
+          const uint32_t ws[4] = {w0, w1, w2, w3};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[e]));
+            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+          }
+        }
+      }
+      qn_l2 = sqrtf(ss) * scale_log2 * 1.001f + 1.0e-3f;
+    }
     for (int r = 0; ok && r < Lx; ++r) {
+      const float kn = (knm != nullptr && r > 0) ? knm[block_of(x, r)] : INFINITY;
       ok = mbar_wait(bars.sfull + x, r & 1, abort_flag, args.status, kStatusTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -387,24 +423,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= valid) s[i] = -INFINITY;
       }
-      float mx[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = max3(s[k], s[8 + k], s[16 + k]);
-#pragma unroll
-      for (int i = 24; i < 128; i += 16) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], s[i + k], s[i + 8 + k]);
-      }
-      const float m_all = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-      const float m_tile = m_all * scale_log2;
       float alpha = 1.f;
       bool rescale = false;
-      if (r == 0) {
-        m_run = m_tile;
-      } else if (m_tile > m_run + kRescaleThreshold) {
-        alpha = fast_exp2(m_run - m_tile);
-        m_run = m_tile;
-        rescale = true;
+      const bool bounded = __all_sync(0xffffffffu, qn_l2 * kn <= m_run + kBoundSlack);  // false at r = 0
+      if (!bounded) {
+        float mx[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = max3(s[k], s[8 + k], s[16 + k]);
+#pragma unroll
+        for (int i = 24; i < 128; i += 16) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], s[i + k], s[i + 8 + k]);
+        }
+        const float m_all = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+        const float m_tile = m_all * scale_log2;
+        if (r == 0) {
+          m_run = m_tile;
+        } else if (m_tile > m_run + kRescaleThreshold) {
+          alpha = fast_exp2(m_run - m_tile);
+          m_run = m_tile;
+          rescale = true;
+        }
       }
       const float neg_m = -m_run;
       float sum[4] = {0.f, 0.f, 0.f, 0.f};

@@ -37,6 +37,8 @@ struct GatherArgs {
   int rank;                     // 0 < rank < D, rank <= gather_max_rank()
   float* variance;              // [banks, nB, D] rank-folded per-block variance in the basis (nullable)
   __nv_bfloat16* variance_bf16; // [banks, nB_pad, D] (nullable)
+  float* k_norm_max;            // [banks, NB] largest |k| over the tokens of each block (nullable)
+  float* k_mean_norm;           // [banks, nB] |bf16(kbar)| of each video block (nullable)
 };
 int launch_gather(const GatherArgs& a, cudaStream_t s);
 int gather_max_rank();
@@ -140,6 +142,7 @@ struct FmhaArgs {
   int all_blocks;          // 1: every key block (dense attention)
   float scale_log2;        // softmax scale * log2(e)
   const uint8_t* partition;  // [banks, nB, nB]
+  const float* k_norm_max;   // [banks, NB] largest |k| per key block (nullable: always exact maxima)
   int epilogue;            // 0: O and LSE; 1: corrected merge
   const int* out_pos;      // [S] output row of reordered row r (nullptr: r)
   __nv_bfloat16* o;        // [banks, S, D]

@@ -15,6 +15,8 @@
 //    population variances of K U[:, c]; every other column is their mean, which for an
 //    orthonormal U equals (trace of the block covariance - the leading variances) /
 //    (D - rank), so only K U[:, :rank] is formed.
+//  * the norm bounds the softmax kernels use to skip their running-max work: the
+//    largest |k| over each block's tokens and |bf16(kbar)| of each video block.
 // Rows past S (up to S_pad) are written as zeros.  HBM-bound.
 #include "common.cuh"
 #include "kernels.h"
@@ -95,6 +97,7 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
     for (int p = 0; p < PASSES; ++p)
       v[p] = nat[p] >= 0 ? ld_stream_v4(base + static_cast<int64_t>(nat[p]) * a.stride_s[t]) : make_uint4(0, 0, 0, 0);
   };
+  float knorm2 = 0.f;  // largest |k|^2 over this thread's rows
   auto process = [&](int t, const uint4 (&v)[PASSES]) {
     if (a.src[t] == nullptr) return;
     float acc[8];
@@ -115,8 +118,21 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
         *reinterpret_cast<uint4*>(vtile + rl * VSTRIDE + ch * 8) = val;
       }
       if (rl < video_rows) add8(acc, val);
+      if (t == 1 && a.k_norm_max) {
+        // |k|^2 of row rl: this lane's 8 dims, summed over the 16 lanes of the row
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&val);
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+        }
+#pragma unroll
+        for (int o = CPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        knorm2 = fmaxf(knorm2, ss);
+      }
     }
-    const bool want_mean = blk < a.nB && (a.mean[t] != nullptr || (t == 1 && need_k_tile));
+    const bool want_mean = blk < a.nB && (a.mean[t] != nullptr || (t == 1 && (need_k_tile || a.k_mean_norm)));
     if (want_mean) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) red[rsub * D + ch * 8 + e] = acc[e];
@@ -126,7 +142,16 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
 #pragma unroll 4
         for (int g = 0; g < RPP; ++g) sum += red[g * D + tid];
         const float m = sum / static_cast<float>(video_rows);
-        if (t == 1) kmean_s[tid] = m;
+        if (t == 1) {
+          kmean_s[tid] = m;
+          if (a.k_mean_norm) {
+            // |bf16(kbar)|^2 over the D columns (threads 0 .. D-1, whole warps)
+            const float mb = __bfloat162float(__float2bfloat16_rn(m));
+            float q = mb * mb;
+            for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+            if ((tid & 31) == 0) stat[32 + (tid >> 5)] = q;
+          }
+        }
         if (a.mean[t]) a.mean[t][(static_cast<size_t>(bank) * a.nB + blk) * D + tid] = m;
         if (t == 1 && a.kmean_bf16)
           a.kmean_bf16[(static_cast<size_t>(bank) * a.nB_pad + blk) * D + tid] = __float2bfloat16_rn(m);
@@ -134,6 +159,11 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
           a.vmean_t_bf16[(static_cast<size_t>(bank) * D + tid) * a.nB_pad + blk] = __float2bfloat16_rn(m);
       }
       __syncthreads();
+      if (t == 1 && a.k_mean_norm && tid == 0) {
+        float q = 0.f;
+        for (int w = 0; w < D / 32; ++w) q += stat[32 + w];
+        a.k_mean_norm[static_cast<size_t>(bank) * a.nB + blk] = sqrtf(q);
+      }
     }
   };
   {
@@ -144,6 +174,18 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
     load_rows(2, va);
     process(1, vb);
     process(2, va);
+  }
+  if (a.k_norm_max) {
+    // block maximum of the row norms: warp maxima, then one thread
+    float m2 = knorm2;
+    for (int o = 16; o > 0; o >>= 1) m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, o));
+    if ((tid & 31) == 0) stat[48 + (tid >> 5)] = m2;
+    __syncthreads();
+    if (tid == 0) {
+      float mm = 0.f;
+      for (int w = 0; w < kThreads / 32; ++w) mm = fmaxf(mm, stat[48 + w]);
+      a.k_norm_max[static_cast<size_t>(bank) * (a.S_pad / 128) + blk] = sqrtf(mm);
+    }
   }
 
   __syncthreads();  // the staged V and K tiles are complete before anyone reads them back

@@ -260,7 +260,8 @@ class Operator:
         lse = torch.empty(sh.banks, sh.S, dtype=torch.float32, device=dev)
         self.launches.run(
             "recap_block_sparse_fmha", 1,
-            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), None, sh.banks, sh.S, sh.D,
+            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), None, _lib.ptr(inputs.k_norm_max),
+            sh.banks, sh.S, sh.D,
             sh.n_video, 1, float(scale), _lib.ptr(gather_rows(self.layout, dev)) if native else None,
             _lib.ptr(out), _lib.ptr(lse), _lib.ptr(status), _lib.stream_handle(dev),
         )
@@ -274,7 +275,8 @@ class Operator:
         lse = torch.empty(sh.banks, sh.S, dtype=torch.float32, device=dev)
         self.launches.run(
             "recap_block_sparse_fmha", 1,
-            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(partition), sh.banks,
+            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(partition),
+            _lib.ptr(inputs.k_norm_max), sh.banks,
             sh.S, sh.D, sh.n_video, 0, float(scale), None, _lib.ptr(out), _lib.ptr(lse), _lib.ptr(status),
             _lib.stream_handle(dev),
         )
@@ -389,7 +391,8 @@ class Operator:
         out = torch.empty(sh.batch, sh.heads, sh.S, sh.D, dtype=torch.bfloat16, device=dev)
         self.launches.run(
             "recap_sparse_step", 1,
-            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(bank.partition), sh.banks,
+            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(bank.partition),
+            _lib.ptr(inputs.k_norm_max), sh.banks,
             sh.S, sh.D, sh.n_video, float(scale), _lib.ptr(coarse), _lib.ptr(coarse_lse), _lib.ptr(bank.value),
             _lib.ptr(bank.log_mass), _lib.ptr(bank.coarse_lse), _lib.ptr(center),
             _lib.ptr(gather_rows(self.layout, dev)), _lib.ptr(out), _lib.ptr(status), _lib.stream_handle(dev),

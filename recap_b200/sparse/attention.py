@@ -110,6 +110,8 @@ class LayerInputs:
     k_centred_t: torch.Tensor | None = None  # [banks, D, S_pad] bf16, block-centred video keys
     variance: torch.Tensor | None = None  # [banks, nB, D] fp32 rank-folded (when the basis was known)
     variance_bf16: torch.Tensor | None = None  # [banks, nB_pad, D]
+    k_norm_max: torch.Tensor | None = None  # [banks, NB] fp32 largest |k| per 128-token block
+    k_mean_norm: torch.Tensor | None = None  # [banks, nB] fp32 |bf16(kbar)| per video block
 
 
 class Launches:
@@ -186,8 +188,9 @@ class SparseAttention:
         q_r = torch.empty(sh.banks, sh.S_pad, sh.D, dtype=bf, device=dev)
         k_r = torch.empty_like(q_r)
         v_t = torch.empty(sh.banks, sh.D, sh.S_pad, dtype=bf, device=dev)
-        qm = km = vm = kmb = vmtb = kct = var = var_bf16 = None
+        qm = km = vm = kmb = vmtb = kct = var = var_bf16 = kmn = None
         basis = None
+        knm = torch.empty(sh.banks, sh.S_pad // 128, dtype=torch.float32, device=dev)
         rank = int(self.config.closure_rank)
         if means:
             f32 = torch.float32
@@ -197,6 +200,7 @@ class SparseAttention:
             kmb = torch.zeros(sh.banks, sh.nB_pad, sh.D, dtype=bf, device=dev)
             vmtb = torch.zeros(sh.banks, sh.D, sh.nB_pad, dtype=bf, device=dev)
             kct = torch.empty(sh.banks, sh.D, sh.S_pad, dtype=bf, device=dev)
+            kmn = torch.empty(sh.banks, sh.nB, dtype=f32, device=dev)
             if (self._basis is not None and 0 < rank < sh.D and rank <= _lib.load().recap_gather_max_rank()
                     and self._basis.shape == (sh.banks, sh.D, sh.D)):
                 basis = self._basis
@@ -209,9 +213,9 @@ class SparseAttention:
             sh.batch, sh.heads, sh.S, sh.D, sh.n_video, _lib.ptr(gather_rows(layout, dev)),
             _lib.ptr(q_r), _lib.ptr(k_r), _lib.ptr(v_t), _lib.ptr(qm), _lib.ptr(km), _lib.ptr(vm),
             _lib.ptr(kmb), _lib.ptr(vmtb), _lib.ptr(kct), _lib.ptr(basis), rank if basis is not None else 0,
-            _lib.ptr(var), _lib.ptr(var_bf16), _lib.stream_handle(dev),
+            _lib.ptr(var), _lib.ptr(var_bf16), _lib.ptr(knm), _lib.ptr(kmn), _lib.stream_handle(dev),
         )
-        return LayerInputs(sh, q_r, k_r, v_t, qm, km, vm, kmb, vmtb, kct, var, var_bf16)
+        return LayerInputs(sh, q_r, k_r, v_t, qm, km, vm, kmb, vmtb, kct, var, var_bf16, knm, kmn)
 
     # -- the partition --------------------------------------------------------------------
 

@@ -127,15 +127,15 @@ def test_pool_select_ties_take_lower_index():
     assert part[0, 0].cpu().tolist() == [False, True, True, False, False, False, False, True]
 
 
-def _fmha(q_r, k_r, v_t, part, banks, S, d, nv, all_blocks, out_pos=None, native_out=None):
+def _fmha(q_r, k_r, v_t, part, banks, S, d, nv, all_blocks, out_pos=None, native_out=None, knm=None):
     from recap_b200 import _lib as lib
 
     out = torch.empty(banks, S, d, dtype=torch.bfloat16, device=DEV) if native_out is None else native_out
     lse = torch.empty(banks, S, dtype=torch.float32, device=DEV)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
-    lib.call("recap_block_sparse_fmha", lib.ptr(q_r), lib.ptr(k_r), lib.ptr(v_t), lib.ptr(part), banks, S, d, nv,
-             int(all_blocks), 1 / math.sqrt(d), lib.ptr(out_pos), lib.ptr(out), lib.ptr(lse), lib.ptr(status),
-             lib.stream_handle(torch.device(DEV)))
+    lib.call("recap_block_sparse_fmha", lib.ptr(q_r), lib.ptr(k_r), lib.ptr(v_t), lib.ptr(part), lib.ptr(knm), banks,
+             S, d, nv, int(all_blocks), 1 / math.sqrt(d), lib.ptr(out_pos), lib.ptr(out), lib.ptr(lse),
+             lib.ptr(status), lib.stream_handle(torch.device(DEV)))
     torch.cuda.synchronize()
     assert int(status.item()) == 0, f"device status {int(status.item())}"
     return out, lse
@@ -148,7 +148,7 @@ def test_fmha_dense_vs_torch_fp32(d, nv, text):
     q, k, v = _strided_qkv(1, 2, nv + text, d, seed=3)
     _, inp = _run_gather(lay, q, k, v, q_mean=False)
     sh = inp.shapes
-    out, lse = _fmha(inp.q, inp.k, inp.v_t, None, sh.banks, sh.S, d, nv, True)
+    out, lse = _fmha(inp.q, inp.k, inp.v_t, None, sh.banks, sh.S, d, nv, True, knm=inp.k_norm_max)
     qr = inp.q[:, : sh.S].float()
     kr = inp.k[:, : sh.S].float()
     vr = inp.v_t[:, :, : sh.S].transpose(1, 2).float()
@@ -163,9 +163,18 @@ def test_fmha_dense_vs_torch_fp32(d, nv, text):
 
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("nv,text,text_first", [(2048, 0, False), (700, 50, True), (504, 40, False)])
-def test_fmha_block_sparse_vs_oracle(d, nv, text, text_first):
+@pytest.mark.parametrize("bound", ["exact", "bounded", "outliers"])
+def test_fmha_block_sparse_vs_oracle(d, nv, text, text_first, bound):
+    """exact: every block computes its row maximum; bounded: blocks within the |q| |k|
+    bound of the running maximum skip it; outliers: a few keys scaled up 60x make the bound
+    fail for some warps and blocks, which then fall back to the exact path."""
     lay = _layout(nv, text, text_first)
     q, k, v = _strided_qkv(1, 2, nv + text, d, seed=4)
+    if bound == "outliers":
+        g0 = torch.Generator().manual_seed(40)
+        idx = torch.randperm(nv + text, generator=g0)[:7]
+        k = k.clone()
+        k[:, :, idx] *= 60.0
     _, inp = _run_gather(lay, q, k, v, q_mean=False)
     sh = inp.shapes
     g = torch.Generator().manual_seed(5)
@@ -173,7 +182,8 @@ def test_fmha_block_sparse_vs_oracle(d, nv, text, text_first):
     if nv % 128:
         part[:, -1, :] = True
         part[:, :, -1] = True
-    out, lse = _fmha(inp.q, inp.k, inp.v_t, part.to(DEV), sh.banks, sh.S, d, nv, False)
+    knm = None if bound == "exact" else inp.k_norm_max
+    out, lse = _fmha(inp.q, inp.k, inp.v_t, part.to(DEV), sh.banks, sh.S, d, nv, False, knm=knm)
     kmask = orc.kernel_block_mask(part, sh.S, nv)
     ro, rl = orc.masked_attention(inp.q[:, : sh.S].float().cpu(), inp.k[:, : sh.S].float().cpu(),
                                   inp.v_t[:, :, : sh.S].transpose(1, 2).float().cpu(), kmask, 1 / math.sqrt(d))
@@ -201,7 +211,7 @@ def test_fmha_uneven_pairs_vs_oracle(d):
     part = torch.rand(sh.banks, sh.nB, sh.nB, generator=g) < dens
     part[:, -1, :] = True
     part[:, :, -1] = True
-    out, lse = _fmha(inp.q, inp.k, inp.v_t, part.to(DEV), sh.banks, sh.S, d, nv, False)
+    out, lse = _fmha(inp.q, inp.k, inp.v_t, part.to(DEV), sh.banks, sh.S, d, nv, False, knm=inp.k_norm_max)
     kmask = orc.kernel_block_mask(part, sh.S, nv)
     ro, rl = orc.masked_attention(inp.q[:, : sh.S].float().cpu(), inp.k[:, : sh.S].float().cpu(),
                                   inp.v_t[:, :, : sh.S].transpose(1, 2).float().cpu(), kmask, 1 / math.sqrt(d))
@@ -209,6 +219,22 @@ def test_fmha_uneven_pairs_vs_oracle(d):
     assert err <= 2e-2, f"O max abs err {err}"
     lerr = (lse.cpu() - rl).abs().max().item()
     assert lerr <= 2e-3, f"LSE max abs err {lerr}"
+
+
+def test_layout_key_norm_bounds():
+    """The layout pass's norm bounds: the largest |k| over each 128-token block (text
+    included) and |bf16(kbar)| of each video block."""
+    nv, text, d = 700, 50, 128
+    lay = _layout(nv, text, True)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=41)
+    _, inp = _run_gather(lay, q, k, v, q_mean=False)
+    torch.cuda.synchronize()
+    sh = inp.shapes
+    kr = inp.k.float().cpu()  # [banks, S_pad, d], zero past S
+    ref = kr.norm(dim=-1).reshape(sh.banks, -1, 128).amax(-1)
+    assert torch.allclose(inp.k_norm_max.cpu(), ref, rtol=1e-5, atol=1e-5)
+    kb = inp.k_mean.cpu().to(torch.bfloat16).float().norm(dim=-1)
+    assert torch.allclose(inp.k_mean_norm.cpu(), kb, rtol=1e-5, atol=1e-5)
 
 
 def test_exp2_poly_vs_exp2f():
