@@ -145,10 +145,14 @@ int recap_basis_prep(const float* basis, int banks, int D, void* basis_t_bf16, v
  *   rank           the closure rank variance_bf16 is folded at (its columns >= rank hold
  *                  one value, recap/sparse/closure.py:96-104); 0: not folded.  A folded
  *                  variance lets the quadratic term run over rank + 2 columns.
+ *   k_mean_norm    [banks, nB] from recap_layout_gather (nullable): tiles of block means whose
+ *                  logit bound stays within 2^64 of a row's running maximum skip the
+ *                  per-tile maximum (the same result up to fp32 rounding).
  * nB_pad must not exceed 2048. */
 int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const void* cvk_bf16,
                       const void* k_mean_bf16, const void* variance_bf16, const void* v_mean_t_bf16,
-                      const uint8_t* partition, const float* counts_log, const float* old_lse, int banks,
+                      const uint8_t* partition, const float* counts_log, const float* k_mean_norm,
+                      const float* old_lse, int banks,
                       int S, int D, int n_video, float scale, float theta, int rank, void* out, float* lse,
                       float* center_partial, float* center, int* status, void* stream);
 

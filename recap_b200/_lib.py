@@ -52,8 +52,8 @@ SIGNATURES: dict[str, tuple] = {
     "recap_closure_workspace_floats": (_I64, [_I, _I, _I]),
     "recap_closure_stats": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "recap_basis_prep": (_I, [_P, _I, _I, _P, _P]),
-    "recap_coarse_tail": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _I, _P, _P, _P, _P, _P,
-                               _P]),
+    "recap_coarse_tail": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _I, _P, _P, _P, _P,
+                               _P, _P]),
     "recap_block_sparse_fmha": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P]),
     "recap_sparse_step": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "recap_refresh_partials": (_I, [_I, _I]),

@@ -213,8 +213,9 @@ int recap_basis_prep(const float* basis, int banks, int D, void* basis_t_bf16, v
 
 int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const void* cvk_bf16,
                       const void* k_mean_bf16, const void* variance_bf16, const void* v_mean_t_bf16,
-                      const uint8_t* partition, const float* counts_log, const float* old_lse, int banks,
-                      int S, int D, int n_video, float scale, float theta, int rank, void* out, float* lse,
+                      const uint8_t* partition, const float* counts_log, const float* k_mean_norm,
+                      const float* old_lse, int banks, int S, int D, int n_video, float scale, float theta,
+                      int rank, void* out, float* lse,
                       float* center_partial, float* center, int* status, void* stream) {
   Geom g;
   if (!geom(S, n_video, &g) || !d_ok(D) || banks <= 0) return kErrShape;
@@ -241,6 +242,7 @@ int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const v
   a.theta = theta;
   a.rank = rank < 0 || rank >= D ? 0 : rank;
   a.partition = partition;
+  a.k_mean_norm = k_mean_norm;
   a.counts_log = counts_log;
   a.old_lse = old_lse;
   a.out = static_cast<__nv_bfloat16*>(out);

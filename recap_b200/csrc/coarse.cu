@@ -53,6 +53,9 @@ constexpr int kTileN = 128;         // block means per tile
 constexpr int kMaxBlocks = 2048;    // nB_pad limit (column terms in shared memory)
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kLog2e = 1.4426950408889634f;
+// Largest logit excess over the running max (log2 units) the bounded path accepts
+// (exponentials below 2^64 stay finite in fp32 and bf16 with room for the sums).
+constexpr float kBoundSlack = 64.0f;
 
 // FOLD: the quadratic term over K = 16 * k2 <= 64 (one 64-column atom of w);
 // otherwise over all D columns.
@@ -71,12 +74,13 @@ struct CoarseSmem {
   static constexpr int kKWRing = kQsq + kQsqBytes;
   static constexpr int kVRing = kKWRing + kKWStages * kKW;
   static constexpr int kCol = kVRing + kVStages * kOpV;       // fp32 column terms [kMaxBlocks]
-  static constexpr int kXchg = kCol + kMaxBlocks * 4;  // row maxima [2 parity][2 halves][128]
+  static constexpr int kTileKn = kCol + kMaxBlocks * 4;  // largest |kbar| per tile [kMaxBlocks / 128]
+  static constexpr int kXchg = kTileKn + (kMaxBlocks / 128) * 4;  // row maxima [2 slots][2 halves][128]
   static constexpr int kSums = kXchg + 2 * 2 * 128 * 4;  // (l, g) per half [2][2][128], then T partials [128]
   static constexpr int kBars = kSums + (2 * 2 * 128 + 128) * 4;
   // pro_full, pro_mma, qsq_ready, kw_full[2], kw_empty[2], v_full[2], v_empty[2],
-  // s1full[2], s2full, s2free, pfull, ofull, c_full, xfull, done, xchg[2], xsum, tpart
-  static constexpr int kNumBars = 3 + 8 + 2 + 7 + 4;
+  // s1full[2], s2full, s2free, pfull, ofull, c_full, xfull, done, xsum, tpart, xchg[2 slots][4 quarters]
+  static constexpr int kNumBars = 3 + 8 + 2 + 7 + 2 + 8;
   static constexpr int kMisc = kBars + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16 + 4 * 4;
   static_assert(kOpV >= D * D * 2, "U^T is staged in a vbar^T slot");
@@ -106,9 +110,9 @@ __device__ __forceinline__ CoarseBars carve(uint8_t* base) {
   r.c_full = b + 17;
   r.xfull = b + 18;
   r.done = b + 19;
-  r.xchg = b + 20;  // [2]
-  r.xsum = b + 22;
-  r.tpart = b + 23;
+  r.xsum = b + 20;
+  r.tpart = b + 21;
+  r.xchg = b + 22;  // [slot * 4 + lane quarter]
   return r;
 }
 
@@ -130,6 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + L::kVRing;
   float* colterm = reinterpret_cast<float*>(smem + L::kCol);
   float* rowmax = reinterpret_cast<float*>(smem + L::kXchg);
+  float* tile_kn = reinterpret_cast<float*>(smem + L::kTileKn);
   float* rowsums = reinterpret_cast<float*>(smem + L::kSums);
   CoarseBars bars = carve(smem + L::kBars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
@@ -159,8 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bars.s2full, 1);
     mbar_init(bars.s2free, 8);
     mbar_init(bars.pfull, 8);
-    mbar_init(bars.xchg, 8);
-    mbar_init(bars.xchg + 1, 8);
+    for (int i = 0; i < 8; ++i) mbar_init(bars.xchg + i, 2);  // the two warps of a lane quarter
     mbar_init(bars.xsum, 8);
     mbar_init(bars.tpart, 4);
     mbar_init(bars.ofull, 1);
@@ -171,11 +175,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
+  if (threadIdx.x < kMaxBlocks / 128) tile_kn[threadIdx.x] = 0.f;
+  __syncthreads();
   {
-    // per-column term (log2 units): ln n_j for omitted blocks, -inf for kept or padding
+    // per-column term (log2 units): ln n_j for omitted blocks, -inf for kept or padding;
+    // the largest |bf16(kbar_j)| of every tile of 128 block means
     const uint8_t* prow = a.partition + (static_cast<size_t>(bank) * nB + qb) * nB;
-    for (int j = threadIdx.x; j < a.nB_pad; j += kThreads)
-      colterm[j] = (j < nB && prow[j] == 0) ? a.counts_log[j] * kLog2e : -INFINITY;
+    const float* kmn = a.k_mean_norm ? a.k_mean_norm + static_cast<size_t>(bank) * nB : nullptr;
+    for (int base = 0; base < a.nB_pad; base += kThreads) {
+      const int j = base + threadIdx.x;
+      float kn = 0.f;
+      if (j < a.nB_pad) {
+        colterm[j] = (j < nB && prow[j] == 0) ? a.counts_log[j] * kLog2e : -INFINITY;
+        if (kmn != nullptr && j < nB) kn = kmn[j];
+      }
+      if (kmn != nullptr) {
+        // one warp's 32 blocks lie in one tile (128 and kThreads are multiples of 32)
+        for (int o = 16; o > 0; o >>= 1) kn = fmaxf(kn, __shfl_xor_sync(0xffffffffu, kn, o));
+        if ((threadIdx.x & 31) == 0 && j < a.nB_pad)
+          atomicMax(reinterpret_cast<int*>(tile_kn + j / kTileN), __float_as_int(kn));  // kn >= 0
+      }
+    }
   }
   __syncthreads();
   tc_fence_after();
@@ -322,8 +342,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t p = t_s1 + (j & 1) * kTileN;
 #pragma unroll
         for (int s = 0; s < kTileN / 16; ++s) {
+          // P of blocks 16 s .. 16 s + 15: half s / 4 keeps its P in the first 32 of its own
+          // 64 S1 columns
           const uint32_t offv = (s >> 2) * (D * 128) + (s & 3) * 32;
-          mma_bf16_ts(t_o, p + 8 * s, sdesc_k_sw128(vb + offv), idesc, (j > 0 || s > 0) ? 1u : 0u);
+          const uint32_t pa = p + (s >> 2) * 64 + (s & 3) * 8;
+          mma_bf16_ts(t_o, pa, sdesc_k_sw128(vb + offv), idesc, (j > 0 || s > 0) ? 1u : 0u);
         }
         mma_commit(bars.ofull);
         mma_commit(bars.v_empty + st);
@@ -462,6 +485,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     float m_run = -INFINITY;  // running max (log2 domain), identical in both halves
     float l_run = 0.f, g_run = 0.f;  // this half's share of the row sum and of the gated mass
+    // Logit bound: s q.kbar_j <= s |q| |kbar_j|, ln n_j <= ln 128, and the gated quadratic
+    // term is at most theta^2 / 2; with the largest |kbar| of a tile this bounds every logit
+    // of the tile.  A warp whose rows all stay within kBoundSlack of the running max skips
+    // the tile's maximum, the exchange with the other half and the rescale; both warps of a
+    // lane quarter see the same |q|, bound and running max, so they decide alike.
+    float qn_l2 = INFINITY;
+    if (ok && a.k_mean_norm != nullptr) {
+      const uint32_t qrow = smem_u32(sQ) + t * 128;  // Q landed: the prologue MMA has read it
+      float ss = 0.f;
+#pragma unroll
+      for (int at = 0; at < D / 64; ++at) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t w0, w1, w2, w3;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                       : "r"(qrow + at * 16384 + ((c ^ (t & 7)) << 4)));
+          const uint32_t ws[4] = {w0, w1, w2, w3};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[e]));
+            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+          }
+        }
+      }
+      qn_l2 = sqrtf(ss) * s_l2 * 1.001f + 1.0e-3f;
+    }
+    const float bound_add = 7.01f + 0.5f * a.theta * a.theta * kLog2e * 1.001f + 0.1f;
+    int n_xchg = 0;  // exchanges this warp pair has made (slot and parity of its barrier)
     for (int j = 0; ok && j < n_tiles; ++j) {
       const int b = j & 1;
       ok = wait_all(bars.s1full + b, (j >> 1) & 1);
@@ -499,34 +551,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bars.s2free);
-      float mx[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = max3(x[k], x[8 + k], x[16 + k]);
-#pragma unroll
-      for (int i = 24; i < kHalf - 8; i += 16) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], x[i + k], x[i + 8 + k]);
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], x[kHalf - 8 + k]);
-      float m_half = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-      // exchange the half maxima (double-buffered by tile parity); this also orders the
-      // other half's S1 reads before this half's P stores into the S1 columns
-      rowmax[(b * 2 + h) * 128 + t] = m_half;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bars.xchg + b);
-      ok = wait_all(bars.xchg + b, (j >> 1) & 1);
-      if (!ok) break;
-      const float m_tile = fmaxf(m_half, rowmax[(b * 2 + (h ^ 1)) * 128 + t]);
       float alpha = 1.f;
       bool rescale = false;
-      if (m_tile != -INFINITY) {
-        if (m_run == -INFINITY) {
-          m_run = m_tile;  // nothing accumulated yet: O, l and g are zero
-        } else if (m_tile > m_run + kRescaleThreshold) {
-          alpha = fast_exp2(m_run - m_tile);
-          m_run = m_tile;
-          rescale = true;
+      const bool bounded =
+          m_run != -INFINITY && __all_sync(0xffffffffu, qn_l2 * tile_kn[j] + bound_add <= m_run + kBoundSlack);
+      if (!bounded) {
+        float mx[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = max3(x[k], x[8 + k], x[16 + k]);
+#pragma unroll
+        for (int i = 24; i < kHalf - 8; i += 16) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], x[i + k], x[i + 8 + k]);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], x[kHalf - 8 + k]);
+        float m_half = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+        // exchange the half maxima with the other warp of this lane quarter (double-buffered
+        // by the parity of the exchange count)
+        const int slot = n_xchg & 1;
+        rowmax[(slot * 2 + h) * 128 + t] = m_half;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bars.xchg + slot * 4 + q4);
+        ok = wait_all(bars.xchg + slot * 4 + q4, (n_xchg >> 1) & 1);
+        if (!ok) break;
+        ++n_xchg;
+        const float m_tile = fmaxf(m_half, rowmax[(slot * 2 + (h ^ 1)) * 128 + t]);
+        if (m_tile != -INFINITY) {
+          if (m_run == -INFINITY) {
+            m_run = m_tile;  // nothing accumulated yet: O, l and g are zero
+          } else if (m_tile > m_run + kRescaleThreshold) {
+            alpha = fast_exp2(m_run - m_tile);
+            m_run = m_tile;
+            rescale = true;
+          }
         }
       }
       // O must hold P.V(j-1) before it is rescaled; P.V(j) starts after pfull below
@@ -562,8 +620,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           add2(gs[0], gs[1], g0, g1);
           pk[i] = pack_bf16(p0, p1);
         }
-        // P of blocks 64h + 32c .. + 31 (two per column)
-        tmem_st16(t_s1 + b * kTileN + h * (kHalf / 2) + c * 16 + lane_base, pk);
+        // P of blocks 64h + 32c .. + 31 (two per column), in this half's own S1 columns
+        tmem_st16(t_s1 + b * kTileN + h * kHalf + c * 16 + lane_base, pk);
       }
       tmem_wait_st();
       tc_fence_before();

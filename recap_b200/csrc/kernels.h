@@ -115,6 +115,7 @@ struct CoarseArgs {
   float scale, theta;
   int rank;                      // w is folded at this rank (columns >= rank equal); 0: not folded
   const uint8_t* partition;      // [banks, nB, nB]
+  const float* k_mean_norm;      // [banks, nB] |bf16(kbar)| (nullable: exact maxima every tile)
   const float* counts_log;       // [nB] ln(tokens per video block)
   const float* old_lse;          // [banks, rows] coarse LSE at the last refresh (nullable)
   __nv_bfloat16* out;            // [banks, rows, D] coarse O + gate * drift (bf16)

@@ -316,9 +316,14 @@ class SparseAttention:
         *,
         old_lse: torch.Tensor | None = None,
         status: torch.Tensor | None = None,
+        logit_bound: bool = False,
     ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
         """Corrected coarse attention over the blocks ``partition`` omits, for the cached
-        rows; returns (output bf16 [banks, rows, D], lse fp32 [banks, rows], centre or None)."""
+        rows; returns (output bf16 [banks, rows, D], lse fp32 [banks, rows], centre or None).
+        ``logit_bound`` lets tiles of block means within the |q| |kbar| logit bound skip
+        their maximum; it measured slower than the exact path on the bench workload (the
+        exact path exchanges each tile's maximum between the two threads of a row), so it
+        is off by default."""
         sh = inputs.shapes
         dev = inputs.q.device
         out = torch.empty(sh.banks, sh.rows, sh.D, dtype=torch.bfloat16, device=dev)
@@ -335,7 +340,9 @@ class SparseAttention:
             "recap_coarse_tail", 1 + (old_lse is not None),
             _lib.ptr(inputs.q), _lib.ptr(context["basis_t"]), _lib.ptr(context["cvk_bf16"]),
             _lib.ptr(inputs.k_mean_bf16), _lib.ptr(context["variance_bf16"]), _lib.ptr(inputs.v_mean_t_bf16),
-            _lib.ptr(partition), _lib.ptr(counts_log(self.geometry, dev)), _lib.ptr(old_lse),
+            _lib.ptr(partition), _lib.ptr(counts_log(self.geometry, dev)),
+            _lib.ptr(inputs.k_mean_norm if logit_bound else None),
+            _lib.ptr(old_lse),
             sh.banks, sh.S, sh.D, sh.n_video, float(scale), float(self.config.closure_gate_theta),
             int(self.config.closure_rank), _lib.ptr(out), _lib.ptr(lse), _lib.ptr(partial), _lib.ptr(center),
             _lib.ptr(status),

@@ -353,6 +353,15 @@ def test_coarse_tail_vs_oracle(d, nv, text, text_first):
     _check_coarse_tail(d, nv, text, text_first, None)
 
 
+@pytest.mark.parametrize("mode", ["exact", "bounded", "outliers"])
+def test_coarse_tail_bound_paths_vs_oracle(mode):
+    """exact: every tile computes its maximum and exchanges it between the two threads of
+    a row (the operator's default); bounded: tiles within the |q| |kbar| logit bound skip
+    it; outliers: a few keys scaled up 60x make the bound fail for some warps and tiles,
+    which then mix exact and bounded tiles."""
+    _check_coarse_tail(128, 128 * 290 + 77, 50, True, None, mode=mode)
+
+
 @pytest.mark.parametrize("d,rank", [(128, 0), (64, 0), (128, 20), (64, 62), (128, 1)])
 def test_coarse_tail_ranks_vs_oracle(d, rank):
     """The quadratic term over a folded variance (rank + 2 columns, one to four K-steps)
@@ -361,16 +370,22 @@ def test_coarse_tail_ranks_vs_oracle(d, rank):
     _check_coarse_tail(d, 128 * 290 + 77, 50, True, rank)
 
 
-def _check_coarse_tail(d, nv, text, text_first, rank):
+def _check_coarse_tail(d, nv, text, text_first, rank, mode="exact"):
     lay = _layout(nv, text, text_first)
     q, k, v = _strided_qkv(1, 2, nv + text, d, seed=8)
+    if mode == "outliers":
+        g0 = torch.Generator().manual_seed(42)
+        idx = torch.randperm(nv, generator=g0)[:2000]
+        k = k.clone()
+        k[:, :, idx] *= 60.0
     sa, inp = _run_gather(lay, q, k, v, q_mean=True, closure_rank=rank)
     sh = inp.shapes
     scale = 1 / math.sqrt(d)
     part = sa.head_partition(inp, scale)
     ctx = sa.coarse_tail_context(inp, scale)
     old = torch.randn(sh.banks, sh.rows, generator=torch.Generator().manual_seed(9)).to(DEV)
-    out, lse, center = sa.coarse_tail_apply(inp, ctx, part.reshape(sh.banks, sh.nB, sh.nB), scale, old_lse=old)
+    out, lse, center = sa.coarse_tail_apply(inp, ctx, part.reshape(sh.banks, sh.nB, sh.nB), scale, old_lse=old,
+                                            logit_bound=mode != "exact")
     torch.cuda.synchronize()
     q_r = inp.q[:, : sh.S].float().cpu()
     k_r = inp.k[:, : sh.S].float().cpu()
