@@ -101,13 +101,23 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.skip = 0
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"recap_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            # nvidia-smi takes a while to start: begin the timed region once it samples,
+            # and count only the samples taken from then on
+            t0 = time.time()
+            while time.time() - t0 < 5.0:
+                lines = self.path.read_text().count("\n")
+                if lines >= 1:
+                    self.skip = lines
+                    break
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -122,7 +132,7 @@ class ClockSampler:
 
     def summary(self) -> dict:
         try:
-            rows = [r.split(",") for r in self.path.read_text().strip().splitlines()]
+            rows = [r.split(",") for r in self.path.read_text().strip().splitlines()[self.skip:]]
         except Exception:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
         sm = sorted(float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit())

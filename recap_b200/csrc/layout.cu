@@ -37,12 +37,25 @@ __device__ __forceinline__ void add8(float (&acc)[8], const uint4& w) {
   }
 }
 
+// Staged 128 x D bf16 tiles: rows of D * 2 bytes, the 16-byte chunks of row r stored at
+// chunk ^ ((r / 8) mod (D / 8)).  Lanes that read eight consecutive rows of one column
+// (the transposed stores) then see distinct chunks; lanes that read a row see a
+// permutation of its chunks.
+template <int D>
+__device__ __forceinline__ uint32_t stage_off(int r, int chunk) {
+  constexpr int CPR = D / 8;
+  return static_cast<uint32_t>(r * (D * 2) + ((chunk ^ ((r >> 3) & (CPR - 1))) << 4));
+}
+template <int D>
+__device__ __forceinline__ __nv_bfloat16 stage_elem(const uint8_t* tile, int r, int d) {
+  return *reinterpret_cast<const __nv_bfloat16*>(tile + stage_off<D>(r, d >> 3) + (d & 7) * 2);
+}
+
 template <int D>
 struct GatherSmem {
-  static constexpr int VSTRIDE = D + 8;  // padded bf16 row of a staged tile
   static constexpr int kV = 0;
-  static constexpr int kK = kV + 128 * VSTRIDE * 2;
-  static constexpr int kRed = kK + 128 * VSTRIDE * 2;        // [RPP][D] fp32
+  static constexpr int kK = kV + 128 * D * 2;
+  static constexpr int kRed = kK + 128 * D * 2;              // [RPP][D] fp32
   static constexpr int kMean = kRed + 32 * D * 4;            // [D] fp32 key means
   static constexpr int kRot = kMean + D * 4;                 // [128][kMaxRank] fp32
   static constexpr int kStat = kRot + 128 * kMaxRank * 4;    // [2*kMaxRank + 1]
@@ -55,10 +68,9 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
   constexpr int CPR = D / 8;              // 16-byte chunks per row
   constexpr int RPP = kThreads / CPR;     // rows per pass
   constexpr int PASSES = 128 / RPP;
-  constexpr int VSTRIDE = L::VSTRIDE;
   extern __shared__ __align__(16) uint8_t smem[];
-  __nv_bfloat16* vtile = reinterpret_cast<__nv_bfloat16*>(smem + L::kV);
-  __nv_bfloat16* ktile = reinterpret_cast<__nv_bfloat16*>(smem + L::kK);
+  uint8_t* vtile = smem + L::kV;
+  uint8_t* ktile = smem + L::kK;
   float* red = reinterpret_cast<float*>(smem + L::kRed);
   float* kmean_s = reinterpret_cast<float*>(smem + L::kMean);
   float* rot = reinterpret_cast<float*>(smem + L::kRot);
@@ -113,9 +125,9 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
       } else if (t == 1) {
         if (a.kr)
           *reinterpret_cast<uint4*>(a.kr + (static_cast<size_t>(bank) * a.S_pad + r) * D + ch * 8) = val;
-        if (need_k_tile) *reinterpret_cast<uint4*>(ktile + rl * VSTRIDE + ch * 8) = val;
+        if (need_k_tile) *reinterpret_cast<uint4*>(ktile + stage_off<D>(rl, ch)) = val;
       } else if (t == 2) {
-        *reinterpret_cast<uint4*>(vtile + rl * VSTRIDE + ch * 8) = val;
+        *reinterpret_cast<uint4*>(vtile + stage_off<D>(rl, ch)) = val;
       }
       if (rl < video_rows) add8(acc, val);
       if (t == 1 && a.k_norm_max) {
@@ -189,41 +201,46 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
   }
 
   __syncthreads();  // the staged V and K tiles are complete before anyone reads them back
-  if (a.vt != nullptr && a.src[2] != nullptr) {
-    // transposed write: lanes run over d so that the staged reads are conflict-free
-    for (int idx = tid; idx < D * 16; idx += kThreads) {
-      const int d = idx % D;
-      const int kc = idx / D;
-      uint32_t w[4];
+  // Transposed stores (V^T and the centred K^T): for each head dimension d this block
+  // owns 128 contiguous bf16 (256 bytes) of row d.  A half-warp writes one such row, each
+  // lane 8 consecutive tokens (16 bytes); a warp covers two dimensions per step.
+  {
+    const int lane = tid & 31;
+    const int g = lane & 15;   // tokens 8g .. 8g + 7
+    const int dd = lane >> 4;  // which of the warp's two dimensions
+    constexpr int kWarps = kThreads / 32;
+    if (a.vt != nullptr && a.src[2] != nullptr) {
+      for (int d0 = 2 * (tid >> 5); d0 < D; d0 += 2 * kWarps) {
+        const int d = d0 + dd;
+        uint32_t w[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat16 lo = vtile[(kc * 8 + 2 * e) * VSTRIDE + d];
-        const __nv_bfloat16 hi = vtile[(kc * 8 + 2 * e + 1) * VSTRIDE + d];
-        w[e] = static_cast<uint32_t>(__bfloat16_as_ushort(lo)) |
-               (static_cast<uint32_t>(__bfloat16_as_ushort(hi)) << 16);
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat16 lo = stage_elem<D>(vtile, 8 * g + 2 * e, d);
+          const __nv_bfloat16 hi = stage_elem<D>(vtile, 8 * g + 2 * e + 1, d);
+          w[e] = static_cast<uint32_t>(__bfloat16_as_ushort(lo)) |
+                 (static_cast<uint32_t>(__bfloat16_as_ushort(hi)) << 16);
+        }
+        *reinterpret_cast<uint4*>(a.vt + (static_cast<size_t>(bank) * D + d) * a.S_pad + row0 + 8 * g) =
+            make_uint4(w[0], w[1], w[2], w[3]);
       }
-      *reinterpret_cast<uint4*>(a.vt + (static_cast<size_t>(bank) * D + d) * a.S_pad + row0 + kc * 8) =
-          make_uint4(w[0], w[1], w[2], w[3]);
     }
-  }
-
-  if (a.kct != nullptr) {
-    // centred video keys, transposed, bf16; zero outside the video tokens
-    for (int idx = tid; idx < D * 16; idx += kThreads) {
-      const int d = idx % D;
-      const int kc = idx / D;
-      const float m = video_rows > 0 ? kmean_s[d] : 0.f;
-      uint32_t w[4];
+    if (a.kct != nullptr) {
+      // centred video keys, bf16; zero outside the video tokens
+      for (int d0 = 2 * (tid >> 5); d0 < D; d0 += 2 * kWarps) {
+        const int d = d0 + dd;
+        const float m = video_rows > 0 ? kmean_s[d] : 0.f;
+        uint32_t w[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r0 = kc * 8 + 2 * e;
-        const float x0 = r0 < video_rows ? __bfloat162float(ktile[r0 * VSTRIDE + d]) - m : 0.f;
-        const float x1 = r0 + 1 < video_rows ? __bfloat162float(ktile[(r0 + 1) * VSTRIDE + d]) - m : 0.f;
-        const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-        w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        for (int e = 0; e < 4; ++e) {
+          const int r0 = 8 * g + 2 * e;
+          const float x0 = r0 < video_rows ? __bfloat162float(stage_elem<D>(ktile, r0, d)) - m : 0.f;
+          const float x1 = r0 + 1 < video_rows ? __bfloat162float(stage_elem<D>(ktile, r0 + 1, d)) - m : 0.f;
+          const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(a.kct + (static_cast<size_t>(bank) * D + d) * a.S_pad + row0 + 8 * g) =
+            make_uint4(w[0], w[1], w[2], w[3]);
       }
-      *reinterpret_cast<uint4*>(a.kct + (static_cast<size_t>(bank) * D + d) * a.S_pad + row0 + kc * 8) =
-          make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 
@@ -248,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
       if (r < video_rows) {
 #pragma unroll 4
         for (int j = 0; j < D / 8; ++j) {
-          const uint4 w = *reinterpret_cast<const uint4*>(ktile + r * VSTRIDE + j * 8);
+          const uint4 w = *reinterpret_cast<const uint4*>(ktile + stage_off<D>(r, j));
           const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
           float x[8];
 #pragma unroll
@@ -275,24 +292,28 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
     if (tid < D) {
       const float m = kmean_s[tid];
       for (int r = 0; r < video_rows; ++r) {
-        const float x = __bfloat162float(ktile[r * VSTRIDE + tid]) - m;
+        const float x = __bfloat162float(stage_elem<D>(ktile, r, tid)) - m;
         tr = fmaf(x, x, tr);
       }
     }
     for (int o = 16; o > 0; o >>= 1) tr += __shfl_xor_sync(0xffffffffu, tr, o);
     if ((tid & 31) == 0 && tid < D) red[tid >> 5] = tr;
     __syncthreads();
-    if (tid < rank) {
-      // two-pass population variance of column tid of K U
-      float s = 0.f;
-      for (int r = 0; r < video_rows; ++r) s += rot[r * kMaxRank + tid];
-      const float m = s / static_cast<float>(video_rows);
+    if ((tid >> 5) < rank) {
+      // two-pass population variance of column c of K U, one warp per column
+      const int c = tid >> 5;
+      const int lane = tid & 31;
+      float sum = 0.f;
+      for (int r = lane; r < video_rows; r += 32) sum += rot[r * kMaxRank + c];
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const float m = sum / static_cast<float>(video_rows);
       float ss = 0.f;
-      for (int r = 0; r < video_rows; ++r) {
-        const float x = rot[r * kMaxRank + tid] - m;
+      for (int r = lane; r < video_rows; r += 32) {
+        const float x = rot[r * kMaxRank + c] - m;
         ss = fmaf(x, x, ss);
       }
-      stat[tid] = fmaxf(ss / static_cast<float>(video_rows), 0.f);
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) stat[c] = fmaxf(ss / static_cast<float>(video_rows), 0.f);
     }
     __syncthreads();
     if (tid < D) {
