@@ -62,7 +62,8 @@ struct FmhaSmem {
   static constexpr int kMisc = kBars + kNumBars * 8;  // tmem base, abort flag, LA, LB, nS
   static constexpr int kList = kMisc + 32;            // uint16 list_a[2048], only_b[2048]
   static constexpr int kRows = kList + 2 * kMaxKeyBlocks * 2;  // staged partition rows, 2 x 2048 bytes
-  static constexpr int kTotal = kRows + 2 * kMaxKeyBlocks;
+  static constexpr int kCounts = kRows + 2 * kMaxKeyBlocks;   // per-warp list counts [warps][3]
+  static constexpr int kTotal = kCounts + 3 * (kThreads / 32) * 4;
 };
 
 struct Bars {
@@ -169,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint16_t* only_b = list_a + kMaxKeyBlocks;
   uint8_t* row_a = smem + L::kRows;
   uint8_t* row_b = row_a + kMaxKeyBlocks;
+  int* counts = reinterpret_cast<int*>(smem + L::kCounts);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -228,38 +230,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = threadIdx.x; j < args.dense_start; j += kThreads) row_b[j] = p[j];
   }
   __syncthreads();
-  if (warp == 0) {
+  {
+    // Key-block lists by a block-wide compaction: warp w owns a contiguous range of
+    // 32-block chunks; pass 1 counts its blocks kept by both tiles / by A only / by B only,
+    // pass 2 writes them at offsets from the per-warp counts, so every category keeps
+    // ascending block order (shared blocks first in list_a, then A's own).
+    constexpr int kWarps = kThreads / 32;
+    const int n_chunks = (NB + 31) / 32;
+    const int per = (n_chunks + kWarps - 1) / kWarps;
+    const int c0 = warp * per;
+    const int c1 = min(n_chunks, c0 + per);
     const unsigned below = (1u << lane) - 1u;
-    auto kept = [&](int j, bool& ka, bool& kb) {
+    auto masks = [&](int c, unsigned& ms, unsigned& ma, unsigned& mb) {
+      const int j = c * 32 + lane;
       const bool in = j < NB;
       const bool forced = j >= args.dense_start;
-      ka = in && (dense_a || forced || row_a[j] != 0);
-      kb = in && has_b && (dense_b || forced || row_b[j] != 0);
+      const bool ka = in && (dense_a || forced || row_a[j] != 0);
+      const bool kb = in && has_b && (dense_b || forced || row_b[j] != 0);
+      ms = __ballot_sync(0xffffffffu, ka && kb);
+      ma = __ballot_sync(0xffffffffu, ka && !kb);
+      mb = __ballot_sync(0xffffffffu, kb && !ka);
     };
-    int n_shared = 0;
-    for (int base = 0; base < NB; base += 32) {
-      bool ka, kb;
-      kept(base + lane, ka, kb);
-      n_shared += __popc(__ballot_sync(0xffffffffu, ka && kb));
-    }
     int cs = 0, ca = 0, cb = 0;
-    for (int base = 0; base < NB; base += 32) {
-      const int j = base + lane;
-      bool ka, kb;
-      kept(j, ka, kb);
-      const unsigned ms = __ballot_sync(0xffffffffu, ka && kb);
-      const unsigned ma = __ballot_sync(0xffffffffu, ka && !kb);
-      const unsigned mb = __ballot_sync(0xffffffffu, kb && !ka);
-      if (ka && kb) list_a[cs + __popc(ms & below)] = static_cast<uint16_t>(j);
-      if (ka && !kb) list_a[n_shared + ca + __popc(ma & below)] = static_cast<uint16_t>(j);
-      if (kb && !ka) only_b[cb + __popc(mb & below)] = static_cast<uint16_t>(j);
+    for (int c = c0; c < c1; ++c) {
+      unsigned ms, ma, mb;
+      masks(c, ms, ma, mb);
       cs += __popc(ms);
       ca += __popc(ma);
       cb += __popc(mb);
     }
     if (lane == 0) {
-      lens[0] = n_shared + ca;
-      lens[1] = has_b ? n_shared + cb : 0;
+      counts[3 * warp] = cs;
+      counts[3 * warp + 1] = ca;
+      counts[3 * warp + 2] = cb;
+    }
+    __syncthreads();
+    int os = 0, oa = 0, ob = 0, n_shared = 0, ta = 0, tb = 0;
+    for (int w = 0; w < kWarps; ++w) {
+      const int ws = counts[3 * w], wa = counts[3 * w + 1], wb = counts[3 * w + 2];
+      n_shared += ws;
+      ta += wa;
+      tb += wb;
+      if (w < warp) {
+        os += ws;
+        oa += wa;
+        ob += wb;
+      }
+    }
+    oa += n_shared;
+    for (int c = c0; c < c1; ++c) {
+      unsigned ms, ma, mb;
+      masks(c, ms, ma, mb);
+      const uint16_t j = static_cast<uint16_t>(c * 32 + lane);
+      if ((ms >> lane) & 1u) list_a[os + __popc(ms & below)] = j;
+      if ((ma >> lane) & 1u) list_a[oa + __popc(ma & below)] = j;
+      if ((mb >> lane) & 1u) only_b[ob + __popc(mb & below)] = j;
+      os += __popc(ms);
+      oa += __popc(ma);
+      ob += __popc(mb);
+    }
+    if (threadIdx.x == 0) {
+      lens[0] = n_shared + ta;
+      lens[1] = has_b ? n_shared + tb : 0;
       lens[2] = n_shared;
     }
   }
