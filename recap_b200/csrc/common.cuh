@@ -256,6 +256,37 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t addr) {
          | (static_cast<uint64_t>(2) << 61);            // swizzle mode: 128B
 }
 
+// The same descriptor in two 32-bit halves.  The high half is a constant and the low
+// half holds the start-address field, so the descriptor of a K step at byte offset
+// `off` into a tile is the tile's low half + off / 16 (the field cannot carry: shared
+// memory addresses stay below 2^18 bytes).  Used where an issuing thread should spend
+// one add per operand between two MMAs.
+constexpr uint32_t kSdescSw128Hi = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t sdesc_sw128_lo(uint32_t addr) { return ((addr >> 4) & 0x3FFFu) | (1u << 16); }
+
+__device__ __forceinline__ void mma_bf16_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %5};\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kSdescSw128Hi)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kSdescSw128Hi)
+      : "memory");
+}
+
 // Byte offset of element (row, k) of a bf16 K-major tile with `rows` rows in the
 // 128B-swizzled layout written by TMA (box of 64 elements x rows per atom column).
 __device__ __forceinline__ uint32_t sw128_offset(int row, int k, int rows) {

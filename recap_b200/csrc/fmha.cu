@@ -342,8 +342,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && LA + LB > 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, D);
-      const uint32_t q_base = smem_u32(sQ);
-      const uint32_t kv_base = smem_u32(sKV);
+      const uint32_t q_lo = sdesc_sw128_lo(smem_u32(sQ));    // + x * kTileBytes / 16 for Q_x
+      const uint32_t kv_lo = sdesc_sw128_lo(smem_u32(sKV));  // + slot * kTileBytes / 16
       int load_no = 0;
       int slot_k = 0, slot_v = 0;  // latest slot of each kind (K for S, V^T for PV)
       if (mbar_wait(bars.qfull, 0, abort_flag, args.status, kStatusTimeoutTma)) {
@@ -363,14 +363,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             slot = kind == kOpS ? slot_k : slot_v;
           }
           const uint32_t t_sx = tmem + 128 * x;
-          const uint32_t tile = kv_base + slot * kTileBytes;
+          const uint32_t tile_lo = kv_lo + slot * (kTileBytes >> 4);
           if (kind == kOpS) {
             tc_fence_after();
-            const uint32_t qx = q_base + x * kTileBytes;
+            const uint32_t qx_lo = q_lo + x * (kTileBytes >> 4);
 #pragma unroll
             for (int s = 0; s < D / 16; ++s) {
-              const uint32_t off = (s >> 2) * (128 * 128) + (s & 3) * 32;
-              mma_bf16_ss(t_sx, sdesc_k_sw128(qx + off), sdesc_k_sw128(tile + off), idesc_s, s > 0);
+              const uint32_t off = ((s >> 2) * (128 * 128) + (s & 3) * 32) >> 4;
+              mma_bf16_ss_lo(t_sx, qx_lo + off, tile_lo + off, idesc_s, s > 0);
             }
             mma_commit(bars.sfull + x);
           } else {
@@ -379,8 +379,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t t_ox = tmem + 256 + D * x;
 #pragma unroll
             for (int s = 0; s < 8; ++s) {
-              const uint32_t off_v = (s >> 2) * (D * 128) + (s & 3) * 32;
-              mma_bf16_ts(t_ox, t_sx + 8 * s, sdesc_k_sw128(tile + off_v), idesc_o, (round > 0 || s > 0) ? 1u : 0u);
+              const uint32_t off_v = ((s >> 2) * (D * 128) + (s & 3) * 32) >> 4;
+              mma_bf16_ts_lo(t_ox, t_sx + 8 * s, tile_lo + off_v, idesc_o, (round > 0 || s > 0) ? 1u : 0u);
             }
             if (round == (x == 0 ? LA : LB) - 1) mma_commit(bars.ofin + x);
           }
