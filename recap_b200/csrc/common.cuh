@@ -287,6 +287,54 @@ __device__ __forceinline__ void mma_bf16_ts_lo(uint32_t d_tmem, uint32_t a_tmem,
       : "memory");
 }
 
+// Warp-wide forms: every lane of a converged warp executes them with the same operands
+// and the instruction is predicated on `leader`, which is nonzero in exactly one lane
+// (elect_leader()).  The same lane then issues every MMA and every commit, which the
+// commit needs: it tracks the MMAs of the thread that issues it.
+__device__ __forceinline__ uint32_t elect_leader() {
+  uint32_t is_leader;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(is_leader));
+  return is_leader;
+}
+
+__device__ __forceinline__ void mma_bf16_ss_lo_w(uint32_t leader, uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%2, %6};\n\t"
+      "mov.b64 db, {%3, %6};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "setp.ne.b32 e, %0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], da, db, %4, p;\n\t}" ::"r"(leader),
+      "r"(d_tmem), "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kSdescSw128Hi)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_ts_lo_w(uint32_t leader, uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b64 db;\n\t"
+      "mov.b64 db, {%3, %6};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "setp.ne.b32 e, %0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], db, %4, p;\n\t}" ::"r"(leader),
+      "r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kSdescSw128Hi)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_w(uint32_t leader, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %0, 0;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%1];\n\t}" ::"r"(leader),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Byte offset of element (row, k) of a bf16 K-major tile with `rows` rows in the
 // 128B-swizzled layout written by TMA (box of 64 elements x rows per atom column).
 __device__ __forceinline__ uint32_t sw128_offset(int row, int k, int rows) {

@@ -7,7 +7,8 @@
 // One CTA per (bank, pair of query blocks A and B); 10 warps:
 //   warp 0      TMA producer: both Q tiles, then the K and V^T tiles in the order the
 //               MMA warp consumes them, through a ring of NST shared-memory slots;
-//   warp 1      TMEM allocator and MMA issuer (one thread);
+//   warp 1      TMEM allocator and MMA issuer (the warp runs the issue loop, one
+//               elected lane issues each tcgen05 instruction);
 //   warps 2-5   softmax and epilogue of tile A, warps 6-9 of tile B: one query row per
 //               thread (TMEM lane = row), online softmax in the log2 domain with lazy
 //               rescaling of O.
@@ -339,20 +340,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) mbar_drain(bars.qfull, 0);
   } else if (warp == 1) {
     // ================================================================ MMA issuer
-    if (lane == 0 && LA + LB > 0) {
+    // The whole warp runs the issue loop (uniform values, converged control flow) and
+    // one elected lane issues every MMA and commit.
+    if (LA + LB > 0) {
+      const uint32_t leader = elect_leader();
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, D);
       const uint32_t q_lo = sdesc_sw128_lo(smem_u32(sQ));    // + x * kTileBytes / 16 for Q_x
       const uint32_t kv_lo = sdesc_sw128_lo(smem_u32(sKV));  // + slot * kTileBytes / 16
       int load_no = 0;
       int slot_k = 0, slot_v = 0;  // latest slot of each kind (K for S, V^T for PV)
-      if (mbar_wait(bars.qfull, 0, abort_flag, args.status, kStatusTimeoutTma)) {
+      if (__all_sync(0xffffffffu, mbar_wait(bars.qfull, 0, abort_flag, args.status, kStatusTimeoutTma))) {
         walk_ops(LA, LB, [&](int x, int kind, int round) -> bool {
           const bool reuse = x == 1 && round < nS;
           int slot;
           if (!reuse) {
             slot = load_no % NST;
-            if (!mbar_wait(bars.full + slot, (load_no / NST) & 1, abort_flag, args.status, kStatusTimeoutTma))
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(bars.full + slot, (load_no / NST) & 1, abort_flag, args.status, kStatusTimeoutTma)))
               return false;
             ++load_no;
             if (kind == kOpS)
@@ -370,26 +375,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int s = 0; s < D / 16; ++s) {
               const uint32_t off = ((s >> 2) * (128 * 128) + (s & 3) * 32) >> 4;
-              mma_bf16_ss_lo(t_sx, qx_lo + off, tile_lo + off, idesc_s, s > 0);
+              mma_bf16_ss_lo_w(leader, t_sx, qx_lo + off, tile_lo + off, idesc_s, s > 0);
             }
-            mma_commit(bars.sfull + x);
+            mma_commit_w(leader, bars.sfull + x);
           } else {
-            if (!mbar_wait(bars.pfull + x, round & 1, abort_flag, args.status, kStatusTimeoutMma)) return false;
+            if (!__all_sync(0xffffffffu, mbar_wait(bars.pfull + x, round & 1, abort_flag, args.status, kStatusTimeoutMma)))
+              return false;
             tc_fence_after();
             const uint32_t t_ox = tmem + 256 + D * x;
 #pragma unroll
             for (int s = 0; s < 8; ++s) {
               const uint32_t off_v = ((s >> 2) * (D * 128) + (s & 3) * 32) >> 4;
-              mma_bf16_ts_lo(t_ox, t_sx + 8 * s, tile_lo + off_v, idesc_o, (round > 0 || s > 0) ? 1u : 0u);
+              mma_bf16_ts_lo_w(leader, t_ox, t_sx + 8 * s, tile_lo + off_v, idesc_o, (round > 0 || s > 0) ? 1u : 0u);
             }
-            if (round == (x == 0 ? LA : LB) - 1) mma_commit(bars.ofin + x);
+            if (round == (x == 0 ? LA : LB) - 1) mma_commit_w(leader, bars.ofin + x);
           }
-          if (x == 1 || round >= nS) mma_commit(bars.empty + slot);  // last user of the slot
+          if (x == 1 || round >= nS) mma_commit_w(leader, bars.empty + slot);  // last user of the slot
           return true;
         });
       }
-      // All MMAs issued by this thread complete before TMEM is released.
-      mma_commit(bars.done);
+      // All MMAs issued by the leader complete before TMEM is released.
+      mma_commit_w(leader, bars.done);
       mbar_drain(bars.done, 0);
     }
   } else {
