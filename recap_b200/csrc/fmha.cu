@@ -46,10 +46,12 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when th
 // exponential stays below 2^64, finite in fp32 and bf16 with room for the row sums.
 constexpr float kBoundSlack = 64.0f;
 // Of the 16 column pairs of every 32-key chunk, the ones whose bit is set here take
-// their exponentials from exp2_poly2 on the FP32 pipe instead of the MUFU unit.  Off:
-// with one softmax warp per SM sub-partition and tile the extra FP32 instructions
-// cost more than the MUFU time they free (measured on the bench workload).
-constexpr uint32_t kPolyPairs = 0x0u;
+// their exponentials from exp2_poly2 on the FP32 pipe instead of the MUFU unit.  With
+// the tensor core fed at its full rate, a round's 32 MMAs (2048 clk) and the two tiles'
+// 2 x 128 x 128 exponentials on MUFU (2048 clk at 16 per clock) take the same time;
+// moving a quarter of them to the FP32 pipe makes the softmax the shorter of the two
+// (main loop 103 -> 95 clk per MMA on the bench workload; an eighth: 97, 3/8: 100).
+constexpr uint32_t kPolyPairs = 0x1111u;
 
 template <int D>
 struct FmhaSmem {
