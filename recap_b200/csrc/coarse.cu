@@ -282,10 +282,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ================================================================ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the issue sequence (converged, uniform values); one elected
+    // lane issues every MMA and commit.
+    {
+      const uint32_t leader = elect_leader();
       const uint32_t q0 = smem_u32(sQ), qs0 = smem_u32(sQsq), kw0 = smem_u32(sKW), v0 = smem_u32(sV);
       auto wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
-        return mbar_wait(bar, parity, abort_flag, a.status, code);
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, a.status, code));
       };
       bool ok = wait(bars.pro_full, 0, kStatusTimeoutTma);
       if (ok) {
@@ -297,9 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < D / 16; ++s) {
           const uint32_t offq = (s >> 2) * (128 * 128) + (s & 3) * 32;
           const uint32_t offb = (s >> 2) * (D * 128) + (s & 3) * 32;
-          mma_bf16_ss(t_o, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(ut + offb), idesc, s > 0);
+          mma_bf16_ss_w(leader, t_o, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(ut + offb), idesc, s > 0);
         }
-        mma_commit(bars.pro_mma);
+        mma_commit_w(leader, bars.pro_mma);
       }
       auto issue_s1 = [&](int j) -> bool {
         const int st = j % KWS;
@@ -311,9 +314,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < D / 16; ++s) {
           const uint32_t offq = (s >> 2) * (128 * 128) + (s & 3) * 32;
           const uint32_t offb = (s >> 2) * (kTileN * 128) + (s & 3) * 32;
-          mma_bf16_ss(t_s1 + (j & 1) * kTileN, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(kb + offb), idesc, s > 0);
+          mma_bf16_ss_w(leader, t_s1 + (j & 1) * kTileN, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(kb + offb), idesc, s > 0);
         }
-        mma_commit(bars.s1full + (j & 1));
+        mma_commit_w(leader, bars.s1full + (j & 1));
         return true;
       };
       // S2(j) reads the (kbar, w) slot of tile j last: release it afterwards
@@ -326,10 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < k2; ++s) {
           const uint32_t offq = (s >> 2) * (128 * 128) + (s & 3) * 32;
           const uint32_t offb = (s >> 2) * (kTileN * 128) + (s & 3) * 32;
-          mma_bf16_ss(t_s2, sdesc_k_sw128(qs0 + offq), sdesc_k_sw128(wb + offb), idesc, s > 0);
+          mma_bf16_ss_w(leader, t_s2, sdesc_k_sw128(qs0 + offq), sdesc_k_sw128(wb + offb), idesc, s > 0);
         }
-        mma_commit(bars.s2full);
-        mma_commit(bars.kw_empty + st);
+        mma_commit_w(leader, bars.s2full);
+        mma_commit_w(leader, bars.kw_empty + st);
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
@@ -346,10 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // 64 S1 columns
           const uint32_t offv = (s >> 2) * (D * 128) + (s & 3) * 32;
           const uint32_t pa = p + (s >> 2) * 64 + (s & 3) * 8;
-          mma_bf16_ts(t_o, pa, sdesc_k_sw128(vb + offv), idesc, (j > 0 || s > 0) ? 1u : 0u);
+          mma_bf16_ts_w(leader, t_o, pa, sdesc_k_sw128(vb + offv), idesc, (j > 0 || s > 0) ? 1u : 0u);
         }
-        mma_commit(bars.ofull);
-        mma_commit(bars.v_empty + st);
+        mma_commit_w(leader, bars.ofull);
+        mma_commit_w(leader, bars.v_empty + st);
         return true;
       };
       // S1 of the first tiles do not need qsq (the O columns hold Q U until then).  With
@@ -379,11 +382,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < D / 16; ++s) {
           const uint32_t offq = (s >> 2) * (128 * 128) + (s & 3) * 32;
           const uint32_t offb = (s >> 2) * (D * 128) + (s & 3) * 32;
-          mma_bf16_ss(t_s2, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(cb + offb), idesc, s > 0);
+          mma_bf16_ss_w(leader, t_s2, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(cb + offb), idesc, s > 0);
         }
-        mma_commit(bars.xfull);
+        mma_commit_w(leader, bars.xfull);
       }
-      mma_commit(bars.done);
+      mma_commit_w(leader, bars.done);
       mbar_drain(bars.done, 0);
     }
   } else if (warp >= kSoftmaxWarp0) {

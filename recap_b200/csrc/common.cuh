@@ -335,6 +335,28 @@ __device__ __forceinline__ void mma_commit_w(uint32_t leader, uint64_t* bar) {
       : "memory");
 }
 
+__device__ __forceinline__ void mma_bf16_ss_w(uint32_t leader, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "setp.ne.b32 e, %0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], %2, %3, %4, p;\n\t}" ::"r"(leader),
+      "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_ts_w(uint32_t leader, uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "setp.ne.b32 e, %0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], %3, %4, p;\n\t}" ::"r"(leader),
+      "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Byte offset of element (row, k) of a bf16 K-major tile with `rows` rows in the
 // 128B-swizzled layout written by TMA (box of 64 elements x rows per atom column).
 __device__ __forceinline__ uint32_t sw128_offset(int row, int k, int rows) {
