@@ -525,30 +525,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bars.pfull + x);
       l_run = l_run * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
     }
+    // Epilogue.  The row's indices, the merge scalars and the first two 32-column chunks
+    // of the coarse output and refinement are loaded before the wait for the last P.V, so
+    // their latency overlaps it; chunk c + 2 is loaded while chunk c is merged.
+    const int r = qblock * 128 + t;  // reordered row
+    int pos = r < args.S ? (args.out_pos ? args.out_pos[r] : r) : -1;
+    const bool in_seq = pos >= 0 && pos < args.S;  // a corrupt index writes nothing
+    if (!in_seq) pos = 0;
+    const bool video = args.epilogue == 1 && r < args.rows;
+    const size_t vrow = static_cast<size_t>(it.bank) * args.rows + (video ? r : 0);
+    float gl = 0.f, dl = 0.f, ogl = 0.f, cshift = 0.f;
+    uint4 gpre[2][4], dpre[2][4];
+    auto prefetch = [&](int c, int b) {
+      const uint4* gsrc = reinterpret_cast<const uint4*>(args.go + vrow * D + c * 32);
+      const uint4* dsrc = reinterpret_cast<const uint4*>(args.det + vrow * D + c * 32);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        gpre[b][q] = ld_stream_v4(gsrc + q);
+        dpre[b][q] = ld_stream_v4(dsrc + q);
+      }
+    };
+    if (ok && video && in_seq) {
+      gl = args.gl[vrow];
+      dl = args.dl[vrow];
+      ogl = args.ogl[vrow];
+      cshift = args.center[it.bank];
+      prefetch(0, 0);
+      if (D / 32 > 1) prefetch(1, 1);
+    }
     if (ok) {
       ok = mbar_wait(bars.ofin + x, 0, abort_flag, args.status, kStatusTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
       tc_fence_after();
-      const int r = qblock * 128 + t;  // reordered row
-      int pos = r < args.S ? (args.out_pos ? args.out_pos[r] : r) : -1;
-      const bool in_seq = pos >= 0 && pos < args.S;  // a corrupt index writes nothing
-      if (!in_seq) pos = 0;
       const float inv_l = 1.f / l_run;
       const float lse_h = (m_run + __log2f(l_run)) * 0.69314718055994531f;
       const size_t bank_rows = static_cast<size_t>(it.bank) * args.S;
       __nv_bfloat16* orow = args.o + (bank_rows + pos) * D;
-      const bool video = args.epilogue == 1 && r < args.rows;
       float wh = 1.f, wt = 0.f, ms = 0.f, mc = 0.f, inv_td = 0.f, inv_den = 1.f;
-      size_t vrow = 0;
       if (video) {
         // corrected merge (recap/kernels/detail_cache.py:267-292)
-        vrow = static_cast<size_t>(it.bank) * args.rows + r;
-        const float gl = args.gl[vrow];
-        const float dl = args.dl[vrow];
-        const float ogl = args.ogl[vrow];
-        const float cshift = args.center[it.bank];
         const float admit = expf(-fabsf(gl - ogl - cshift));
         const float cl = gl + dl;
         const float tc = fmaxf(gl, cl);
@@ -562,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         wt = expf(tail_l - common);
         inv_den = 1.f / fmaxf(wh + wt, 1.0e-30f);
       }
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         const int c0 = c * 32;  // first output column of this chunk
         float v[32];
@@ -571,14 +588,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!in_seq) continue;
         float res[32];
         if (video) {
-          const uint4* gsrc = reinterpret_cast<const uint4*>(args.go + vrow * D + c0);
-          const uint4* dsrc = reinterpret_cast<const uint4*>(args.det + vrow * D + c0);
+          uint4 gw4[4], dw4[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const uint4 gw = ld_stream_v4(gsrc + q);
-            const uint4 dw = ld_stream_v4(dsrc + q);
-            const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw);
-            const __half2* d2 = reinterpret_cast<const __half2*>(&dw);
+            gw4[q] = gpre[c & 1][q];
+            dw4[q] = dpre[c & 1][q];
+          }
+          if (c + 2 < D / 32) prefetch(c + 2, c & 1);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw4[q]);
+            const __half2* d2 = reinterpret_cast<const __half2*>(&dw4[q]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 gf = __bfloat1622float2(g2[e]);
