@@ -177,6 +177,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bars.done, 1);
     *abort_flag = 0;
     fence_barrier_init();
+    // the Q tile and U^T depend on nothing computed here: start their loads first
+    const uint64_t stream = l2_evict_first();  // the Q tile: read once here
+    const int qrow = bank * a.S_pad + qb * 128;
+    mbar_expect_tx(bars.pro_full, L::kTileQ + D * D * 2);
+#pragma unroll
+    for (int at = 0; at < D / 64; ++at) {
+      tma_load_2d_hint(sQ + at * 128 * 128, &tm_q, bars.pro_full, at * 64, qrow, stream);
+      // U^T waits in the second vbar^T slot, which the second tile needs last
+      tma_load_2d(sV + (1 % VS) * L::kOpV + at * D * 128, &tm_ut, bars.pro_full, at * 64, bank * D);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   if (threadIdx.x < kMaxBlocks / 128) tile_kn[threadIdx.x] = 0.f;
@@ -213,15 +223,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ================================================================ Q, U^T, (kbar, w), C_vk
     if (lane == 0) {
       const uint64_t keep = l2_evict_last();    // per-bank operands: read by every query block
-      const uint64_t stream = l2_evict_first(); // the Q tile: read once here
-      const int qrow = bank * a.S_pad + qb * 128;
-      mbar_expect_tx(bars.pro_full, kTileQ + D * D * 2);
-#pragma unroll
-      for (int at = 0; at < D / 64; ++at) {
-        tma_load_2d_hint(sQ + at * 128 * 128, &tm_q, bars.pro_full, at * 64, qrow, stream);
-        // U^T waits in the second vbar^T slot, which the second tile needs last
-        tma_load_2d(sV + (1 % VS) * L::kOpV + at * D * 128, &tm_ut, bars.pro_full, at * 64, bank * D);
-      }
       bool ok = true;
       int j = 0;
       for (; ok && j < n_tiles; ++j) {
@@ -367,18 +368,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) ok = wait(bars.qsq_ready, 0, kStatusTimeoutMma);
       if (ok) ok = issue_s2(0);
       if (ok && n_tiles > 1 && KWS == 1) ok = issue_s1(1);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) {
-          ok = wait(bars.s2free, j & 1, kStatusTimeoutMma);
-          if (ok) ok = issue_s2(j + 1);
-        }
-        if (ok) ok = issue_pv(j);
-        if (ok && j + 2 < n_tiles) ok = issue_s1(j + 2);
-      }
       // drift: Q C_vk^T into the S2 columns once the last S2 has been read
-      if (ok) ok = wait(bars.s2free, (n_tiles - 1) & 1, kStatusTimeoutMma);
-      if (ok) ok = wait(bars.c_full, 0, kStatusTimeoutTma);
-      if (ok) {
+      auto issue_drift = [&]() -> bool {
+        if (!wait(bars.s2free, (n_tiles - 1) & 1, kStatusTimeoutMma)) return false;
+        if (!wait(bars.c_full, 0, kStatusTimeoutTma)) return false;
         tc_fence_after();
         constexpr uint32_t idesc = idesc_bf16_f32(128, D);
         const uint32_t cb = kw0 + (n_tiles % KWS) * L::kKW;
@@ -389,6 +382,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_bf16_ss_w(leader, t_s2, sdesc_k_sw128(q0 + offq), sdesc_k_sw128(cb + offb), idesc, s > 0);
         }
         mma_commit_w(leader, bars.xfull);
+        return true;
+      };
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles) {
+          ok = wait(bars.s2free, j & 1, kStatusTimeoutMma);
+          if (ok) ok = issue_s2(j + 1);
+        } else {
+          // the drift goes out while the softmax still works on the last tile, ahead of
+          // the last P.V (it needs only the freed S2 columns, Q and C_vk)
+          ok = issue_drift();
+        }
+        if (ok) ok = issue_pv(j);
+        if (ok && j + 2 < n_tiles) ok = issue_s1(j + 2);
       }
       mma_commit_w(leader, bars.done);
       mbar_drain(bars.done, 0);
@@ -520,6 +526,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       qn_l2 = sqrtf(ss) * s_l2 * 1.001f + 1.0e-3f;
     }
     const float bound_add = 7.01f + 0.5f * a.theta * a.theta * kLog2e * 1.001f + 0.1f;
+    // the epilogue's drift-centre input, loaded now so that its latency is spent here
+    const size_t orow_pre = static_cast<size_t>(bank) * a.rows + (qb * 128 + t);
+    const float old_lse_pre = (h == 0 && a.center_partial != nullptr) ? a.old_lse[orow_pre] : 0.f;
     int n_xchg = 0;  // exchanges this warp pair has made (slot and parity of its barrier)
     for (int j = 0; ok && j < n_tiles; ++j) {
       const int b = j & 1;
@@ -694,7 +703,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (h == 0) {
         a.lse[orow] = lse;
         if (a.center_partial != nullptr) {
-          float dv = lse - a.old_lse[orow];
+          float dv = lse - old_lse_pre;
           for (int o = 16; o > 0; o >>= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
           if (lane == 0) row_part[q4] = dv;
         }
