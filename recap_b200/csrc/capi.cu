@@ -337,6 +337,16 @@ int recap_sparse_step(const void* q_reordered, const void* k_reordered, const vo
   a.ogl = old_lse;
   a.center = center;
   a.status = status;
+  a.tma_epilogue = 0;
+  if (g.rows > 0) {
+    // the epilogue stages each tile's coarse output and refinement through shared memory
+    // (both 2-byte elements: the copies move bytes)
+    const uint64_t vrows = static_cast<uint64_t>(banks) * g.rows;
+    rc = make_tmap_bf16(&L.tm_go, coarse_out, vrows, D, 128);
+    if (rc == kOk) rc = make_tmap_bf16(&L.tm_det, detail_value, vrows, D, 128);
+    if (rc != kOk) return rc;
+    a.tma_epilogue = 1;
+  }
   return launch_fmha(L, static_cast<cudaStream_t>(stream));
 }
 

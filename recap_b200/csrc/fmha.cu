@@ -155,7 +155,8 @@ __device__ __forceinline__ bool walk_ops(int LA, int LB, Op&& op) {
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_vt, const FmhaArgs args) {
+                    const __grid_constant__ CUtensorMap tm_vt, const __grid_constant__ CUtensorMap tm_go,
+                    const __grid_constant__ CUtensorMap tm_det, const FmhaArgs args) {
   using L = FmhaSmem<D>;
   constexpr int NST = L::kNst;
   constexpr uint32_t kTileBytes = L::kTileBytes;
@@ -335,6 +336,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++load_no;
         return true;
       });
+      // The epilogue's coarse output and refinement tiles (one 128-row tile of each per
+      // merged query block) go into the ring slots as they come free, as loads number
+      // n_own, n_own + 1, ... after the walk's n_own loads.
+      if (args.tma_epilogue && !*abort_flag) {
+        const uint64_t stream = l2_evict_first();  // read once
+#pragma unroll 1
+        for (int y = 0; y < 2; ++y) {
+          const int qblock = y == 0 ? it.qa : it.qb;
+          if (qblock < 0 || (qblock + 1) * 128 > args.rows) continue;
+          const int row0 = it.bank * args.rows + qblock * 128;
+#pragma unroll 1
+          for (int k = 0; k < 2; ++k) {
+            const int slot = load_no % NST;
+            if (load_no >= NST &&
+                !mbar_wait(bars.empty + slot, ((load_no / NST) - 1) & 1, abort_flag, args.status,
+                           kStatusTimeoutProducer))
+              break;
+            uint8_t* dst = sKV + slot * kTileBytes;
+            mbar_expect_tx(bars.full + slot, kTileBytes);
+#pragma unroll
+            for (int a = 0; a < D / 64; ++a)
+              tma_load_2d_hint(dst + a * 128 * 128, k == 0 ? &tm_go : &tm_det, bars.full + slot, a * 64, row0, stream);
+            ++load_no;
+          }
+        }
+      }
       // Leave no bulk copy in flight: wait for the last loads this thread issued.
       const int first = load_no > NST ? load_no - NST : 0;
       for (int k = first; k < load_no; ++k) mbar_drain(bars.full + (k % NST), (k / NST) & 1);
@@ -525,106 +552,134 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bars.pfull + x);
       l_run = l_run * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
     }
-    // Epilogue.  The row's indices, the merge scalars and the first two 32-column chunks
-    // of the coarse output and refinement are loaded before the wait for the last P.V, so
-    // their latency overlaps it; chunk c + 2 is loaded while chunk c is merged.
+    // Epilogue.  For a merged (video) query block the coarse output and refinement tiles
+    // arrive by TMA in the freed ring slots; each thread merges its row from shared memory
+    // into the coarse-output slot, then every warp stores its 32 rows as whole 256-byte
+    // rows (two per instruction) at their native positions.  The row's indices and merge
+    // scalars are loaded before the wait for the last P.V, so their latency overlaps it.
     const int r = qblock * 128 + t;  // reordered row
     int pos = r < args.S ? (args.out_pos ? args.out_pos[r] : r) : -1;
-    const bool in_seq = pos >= 0 && pos < args.S;  // a corrupt index writes nothing
-    if (!in_seq) pos = 0;
-    const bool video = args.epilogue == 1 && r < args.rows;
+    const bool video = args.epilogue == 1 && r < args.rows;  // whole blocks: rows is a multiple of 128
     const size_t vrow = static_cast<size_t>(it.bank) * args.rows + (video ? r : 0);
     float gl = 0.f, dl = 0.f, ogl = 0.f, cshift = 0.f;
-    uint4 gpre[2][4], dpre[2][4];
-    auto prefetch = [&](int c, int b) {
-      const uint4* gsrc = reinterpret_cast<const uint4*>(args.go + vrow * D + c * 32);
-      const uint4* dsrc = reinterpret_cast<const uint4*>(args.det + vrow * D + c * 32);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        gpre[b][q] = ld_stream_v4(gsrc + q);
-        dpre[b][q] = ld_stream_v4(dsrc + q);
-      }
-    };
-    if (ok && video && in_seq) {
+    if (ok && video) {
       gl = args.gl[vrow];
       dl = args.dl[vrow];
       ogl = args.ogl[vrow];
       cshift = args.center[it.bank];
-      prefetch(0, 0);
-      if (D / 32 > 1) prefetch(1, 1);
+    }
+    const bool staged = video && args.tma_epilogue;
+    uint32_t s_go = 0, s_det = 0;  // shared addresses of this tile's staged tiles
+    int n_go = 0;                  // load number of this tile's coarse-output tile
+    if (staged) {
+      const int n_own = (LA > 0) + (LB > 0 && nS == 0) + LA + max(0, LA - 1) + max(0, LB - nS) +
+                        max(0, LB - 1 - max(nS - 1, 0));
+      const bool a_merged = (it.qa + 1) * 128 <= args.rows;
+      n_go = n_own + (x == 1 && a_merged ? 2 : 0);
+      s_go = smem_u32(sKV) + (n_go % NST) * kTileBytes;
+      s_det = smem_u32(sKV) + ((n_go + 1) % NST) * kTileBytes;
     }
     if (ok) {
       ok = mbar_wait(bars.ofin + x, 0, abort_flag, args.status, kStatusTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
     }
+    if (ok && staged) {
+      ok = mbar_wait(bars.full + n_go % NST, (n_go / NST) & 1, abort_flag, args.status, kStatusTimeoutSoftmax) &&
+           mbar_wait(bars.full + (n_go + 1) % NST, ((n_go + 1) / NST) & 1, abort_flag, args.status,
+                     kStatusTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+    }
     if (ok) {
       tc_fence_after();
+      const bool in_seq = pos >= 0 && pos < args.S;  // a corrupt index writes nothing
+      if (!in_seq) pos = 0;
       const float inv_l = 1.f / l_run;
       const float lse_h = (m_run + __log2f(l_run)) * 0.69314718055994531f;
       const size_t bank_rows = static_cast<size_t>(it.bank) * args.S;
       __nv_bfloat16* orow = args.o + (bank_rows + pos) * D;
-      float wh = 1.f, wt = 0.f, ms = 0.f, mc = 0.f, inv_td = 0.f, inv_den = 1.f;
-      if (video) {
+      if (staged) {
         // corrected merge (recap/kernels/detail_cache.py:267-292)
         const float admit = expf(-fabsf(gl - ogl - cshift));
         const float cl = gl + dl;
         const float tc = fmaxf(gl, cl);
-        ms = (1.f - admit) * expf(gl - tc);
-        mc = admit * expf(cl - tc);
+        const float ms = (1.f - admit) * expf(gl - tc);
+        const float mc = admit * expf(cl - tc);
         const float td = fmaxf(ms + mc, 1.0e-30f);
-        inv_td = 1.f / td;
+        const float inv_td = 1.f / td;
         const float tail_l = tc + logf(td);
         const float common = fmaxf(lse_h, tail_l);
-        wh = expf(lse_h - common);
-        wt = expf(tail_l - common);
-        inv_den = 1.f / fmaxf(wh + wt, 1.0e-30f);
-      }
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        const int c0 = c * 32;  // first output column of this chunk
-        float v[32];
-        tmem_ld32(t_ox + c0, v);
-        tmem_wait_ld();
-        if (!in_seq) continue;
-        float res[32];
-        if (video) {
-          uint4 gw4[4], dw4[4];
+        const float wh = expf(lse_h - common);
+        const float wt = expf(tail_l - common);
+        const float inv_den = 1.f / fmaxf(wh + wt, 1.0e-30f);
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tmem_ld32(t_ox + c * 32, v);
+          tmem_wait_ld();
+          // row t, columns 32 c .. 32 c + 31: four 16-byte chunks of the 128-byte-swizzled tile
+          const uint32_t row_off = (c >> 1) * (128 * 128) + t * 128;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            gw4[q] = gpre[c & 1][q];
-            dw4[q] = dpre[c & 1][q];
-          }
-          if (c + 2 < D / 32) prefetch(c + 2, c & 1);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw4[q]);
-            const __half2* d2 = reinterpret_cast<const __half2*>(&dw4[q]);
+            const uint32_t off = row_off + (((((c & 1) * 4 + q) ^ (t & 7))) << 4);
+            uint32_t gw[4], dw[4];
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(gw[0]), "=r"(gw[1]), "=r"(gw[2]), "=r"(gw[3])
+                         : "r"(s_go + off));
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(dw[0]), "=r"(dw[1]), "=r"(dw[2]), "=r"(dw[3])
+                         : "r"(s_det + off));
+            uint32_t res[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float2 gf = __bfloat1622float2(g2[e]);
-              const float2 df = __half22float2(d2[e]);
+              const float2 gf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[e]));
+              const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dw[e]));
               const int i0 = 8 * q + 2 * e;
               const float oh0 = bf16_round(v[i0] * inv_l);
               const float oh1 = bf16_round(v[i0 + 1] * inv_l);
               const float to0 = (gf.x * ms + (gf.x + df.x) * mc) * inv_td;
               const float to1 = (gf.y * ms + (gf.y + df.y) * mc) * inv_td;
-              res[i0] = (oh0 * wh + to0 * wt) * inv_den;
-              res[i0 + 1] = (oh1 * wh + to1 * wt) * inv_den;
+              res[e] = pack_bf16((oh0 * wh + to0 * wt) * inv_den, (oh1 * wh + to1 * wt) * inv_den);
             }
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(s_go + off), "r"(res[0]), "r"(res[1]),
+                         "r"(res[2]), "r"(res[3])
+                         : "memory");
           }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) res[i] = v[i] * inv_l;
         }
-        uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+        __syncwarp();
+        // the warp's 32 rows, 256 / (D / 8) rows per instruction, each row whole
+        constexpr int kChunks = D / 8;            // 16-byte chunks per row
+        constexpr int kRowsPer = 32 / kChunks;    // rows per warp instruction
+        const int j = lane % kChunks;
+#pragma unroll 1
+        for (int i0 = 0; i0 < 32; i0 += kRowsPer) {
+          const int i = i0 + lane / kChunks;      // row of the warp this lane stores
+          const int ti = q4 * 32 + i;
+          const int pos_i = __shfl_sync(0xffffffffu, pos, i);
+          const int ok_i = __shfl_sync(0xffffffffu, in_seq ? 1 : 0, i);
+          uint32_t w0, w1, w2, w3;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                       : "r"(s_go + (j >> 3) * (128 * 128) + ti * 128 + (((j & 7) ^ (ti & 7)) << 4)));
+          if (ok_i) st_stream_v4(args.o + (bank_rows + pos_i) * D + j * 8, make_uint4(w0, w1, w2, w3));
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          const int c0 = c * 32;  // first output column of this chunk
+          float v[32];
+          tmem_ld32(t_ox + c0, v);
+          tmem_wait_ld();
+          if (!in_seq) continue;
+          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 w;
-          w.x = pack_bf16(res[8 * q + 0], res[8 * q + 1]);
-          w.y = pack_bf16(res[8 * q + 2], res[8 * q + 3]);
-          w.z = pack_bf16(res[8 * q + 4], res[8 * q + 5]);
-          w.w = pack_bf16(res[8 * q + 6], res[8 * q + 7]);
-          st_stream_v4(dst + q, w);
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16(v[8 * q + 0] * inv_l, v[8 * q + 1] * inv_l);
+            w.y = pack_bf16(v[8 * q + 2] * inv_l, v[8 * q + 3] * inv_l);
+            w.z = pack_bf16(v[8 * q + 4] * inv_l, v[8 * q + 5] * inv_l);
+            w.w = pack_bf16(v[8 * q + 6] * inv_l, v[8 * q + 7] * inv_l);
+            st_stream_v4(dst + q, w);
+          }
         }
       }
       if (in_seq && args.lse) args.lse[bank_rows + pos] = lse_h;
@@ -648,13 +703,13 @@ int launch_fmha(const FmhaLaunch& L, cudaStream_t stream) {
   if (L.D == 128) {
     const int smem = FmhaSmem<128>::kTotal + 1024;
     cudaFuncSetAttribute(fmha_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    fmha_fwd_kernel<128><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, a);
+    fmha_fwd_kernel<128><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.tm_go, L.tm_det, a);
   } else if (L.D == 64) {
     // request enough shared memory for one CTA per SM (TMEM holds one CTA's 512 columns)
     int smem = FmhaSmem<64>::kTotal + 1024;
     if (smem < 120 * 1024) smem = 120 * 1024;
     cudaFuncSetAttribute(fmha_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    fmha_fwd_kernel<64><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, a);
+    fmha_fwd_kernel<64><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.tm_go, L.tm_det, a);
   } else {
     return kErrShape;
   }

@@ -154,11 +154,13 @@ struct FmhaArgs {
   const float* dl;         // [banks, rows] refinement of the tail log-mass
   const float* ogl;        // [banks, rows] coarse LSE at the refresh
   const float* center;     // [banks]
+  int tma_epilogue;        // 1: tm_go / tm_det describe go / det (epilogue 1 with video rows)
   int* status;
 };
 struct FmhaLaunch {
   int D;
   CUtensorMap tm_q, tm_k, tm_vt;
+  CUtensorMap tm_go, tm_det;  // [banks * rows, D] coarse output / refinement, 2-byte elements
   FmhaArgs args;
 };
 int launch_fmha(const FmhaLaunch& L, cudaStream_t s);

@@ -186,3 +186,42 @@ def test_exact_matches_dense_attention():
     out = op.attend(0, q, k, v).float()
     ref = torch.softmax((q.float() @ k.float().transpose(-1, -2)) / 8.0, -1) @ v.float()
     assert float((out - ref).abs().max()) <= MAX_ABS
+
+
+@pytest.mark.parametrize("prefetch", [True, False])
+def test_host_bank_streaming_matches_resident(prefetch):
+    """HostBankOperator with an HBM budget of zero streams each layer's refinement through
+    pinned host memory (two device slots, prefetch and write-back streams); its outputs
+    equal the HBM-resident operator's bit for bit over refresh -> sparse -> sparse ->
+    refresh across three layers (the copies are exact and the kernels are the same)."""
+    from recap_b200 import REFRESH, SPARSE, HostBankOperator, Operator, OperatorConfig
+    from recap_b200.sparse import Layout, SparseGeometry, hilbert_permutation
+
+    spec = SPECS["textlast_d128"]
+    perm = hilbert_permutation(spec["grid"])
+    layout = Layout.from_permutation(perm, text_tokens=spec["text"], text_first=spec["text_first"])
+    geo = SparseGeometry.build(layout, 128)
+    cfg = OperatorConfig(head_density=spec["density"])
+    n_layers = 3
+    resident = Operator.build(cfg, geo, n_layers=n_layers)
+    streamed = HostBankOperator.build(cfg, geo, n_layers=n_layers)
+    streamed.hbm_budget = 0
+    streamed.set_prefetch(prefetch)
+    held = streamed.preallocate_host(n_layers, spec["heads"], spec["dim"])
+    assert streamed.resident is False and held > 0
+
+    bf = torch.bfloat16
+    base = [t.to(bf) for t in _inputs(spec)]
+    steps = [REFRESH, SPARSE, SPARSE, REFRESH]
+    for step, kind in enumerate(steps):
+        for op in (resident, streamed):
+            op.begin_step(step, kind)
+        for layer in range(n_layers):
+            q, k, v = orc.perturb3(*(t.float() for t in base), seed=100 * step + layer)
+            args = [t.to(bf).to(DEV) for t in (q, k, v)]
+            out_r = resident.attend(layer, *args)
+            out_s = streamed.attend(layer, *args)
+            assert torch.equal(out_r, out_s), (step, layer)
+    streamed.finish()
+    resident.check_device_status()
+    streamed.check_device_status()
