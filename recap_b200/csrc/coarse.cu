@@ -12,13 +12,14 @@
 // they replace, P rounded to bf16 before P vbar, the output rounded to bf16 and the
 // drift added in bf16 arithmetic.
 //
-// Rank folding: with 0 < rank and rank + 2 <= 64, the per-block variances w_j are
+// Rank folding: with 0 < rank and rank + 4 <= 64, the per-block variances w_j are
 // folded (recap/sparse/closure.py:96-104): every column c >= rank holds the same tail
 // value.  Then  qsq . w_j = sum_{c<rank} qsq_c w_jc + w_j,rank * T  with
-// T = sum_{c>=rank} qsq_c, and the quadratic term is one MMA over K = 16 (rank <= 14):
-// the A row is (qsq_0 .. qsq_{rank-1}, T_hi, T_lo, 0 ...) with T split into two bf16
-// parts (T_hi + T_lo = T to 2^-17), the B row the first 16 folded columns of w_j.
-// Otherwise the product runs over all D columns.
+// T = sum_{c>=rank} qsq_c, and the quadratic term is one MMA over K = 16 (rank <= 12):
+// the A row is (qsq_0 .. qsq_{rank-1}, T0_hi, T0_lo, T1_hi, T1_lo, 0 ...) with T0 and T1
+// the two column halves' partial tails, each split into two bf16 parts (hi + lo equals
+// the part to 2^-17), the B row the first 16 folded columns of w_j (columns rank ..
+// rank + 3 all hold the tail).  Otherwise the product runs over all D columns.
 //
 // The omitted set is a mask over all nB block means, processed in tiles of 128
 // (kbar, w and vbar^T of a bank stay in L2).  One CTA per (query block, bank),
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nB = a.nB;
   const int n_tiles = a.nB_pad / kTileN;
   // K-steps of the quadratic term
-  const int k2 = FOLD ? (a.rank + 2 + 15) / 16 : D / 16;
+  const int k2 = FOLD ? (a.rank + 4 + 15) / 16 : D / 16;
 
   if (threadIdx.x == 0) {
     mbar_init(bars.pro_full, 1);
@@ -190,6 +191,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   if (threadIdx.x < kMaxBlocks / 128) tile_kn[threadIdx.x] = 0.f;
+  if (FOLD) {
+    // the folded quadratic term's A tile: the columns past the tails stay zero
+    for (int i = threadIdx.x; i < L::kQsqBytes / 16; i += kThreads)
+      reinterpret_cast<uint4*>(sQsq)[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_async_smem();
+  }
   __syncthreads();
   {
     // per-column term (log2 units): ln n_j for omitted blocks, -inf for kept or padding;
@@ -422,8 +429,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 128-byte swizzle); each half squares D/2 columns of q U
       const uint32_t qsq_row = smem_u32(sQsq) + t * 128;
       if (FOLD) {
-        // (qsq_0 .. qsq_{rank-1}, T_hi, T_lo, 0 ...) over 16 k2 columns: each half stores
-        // the qsq_k of its own columns, half 0 the rest
+        // (qsq_0 .. qsq_{rank-1}, T0_hi, T0_lo, T1_hi, T1_lo, 0 ...) over 16 k2 columns:
+        // each half stores the qsq_k of its own columns (rank < 64: all in half 0) and
+        // its partial tail at columns rank + 2h, rank + 2h + 1; the rest was zeroed
         const int rank = a.rank;
         float tail = 0.f;
 #pragma unroll 1
@@ -446,30 +454,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        float* tp = rowsums + 2 * 2 * 128;  // past the (l, g) sums: T partials of half 1
-        if (h == 1) {
-          tp[t] = tail;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bars.tpart);
-        } else {
-          ok = wait_all(bars.tpart, 0);
-          if (ok) {
-            tail += tp[t];
-            const __nv_bfloat16 hi = __float2bfloat16_rn(tail);
-            const __nv_bfloat16 lo = __float2bfloat16_rn(tail - __bfloat162float(hi));
-            const int k_hi = rank, k_lo = rank + 1;
-            asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_hi >> 3) ^ (t & 7)) << 4) + (k_hi & 7) * 2),
-                         "h"(*reinterpret_cast<const unsigned short*>(&hi))
-                         : "memory");
-            asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_lo >> 3) ^ (t & 7)) << 4) + (k_lo & 7) * 2),
-                         "h"(*reinterpret_cast<const unsigned short*>(&lo))
-                         : "memory");
-            for (int k = rank + 2; k < 16 * k2; ++k)
-              asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k >> 3) ^ (t & 7)) << 4) + (k & 7) * 2),
-                           "h"(static_cast<unsigned short>(0))
-                           : "memory");
-          }
-        }
+        const __nv_bfloat16 hi = __float2bfloat16_rn(tail);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(tail - __bfloat162float(hi));
+        const int k_hi = rank + 2 * h, k_lo = rank + 2 * h + 1;
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_hi >> 3) ^ (t & 7)) << 4) + (k_hi & 7) * 2),
+                     "h"(*reinterpret_cast<const unsigned short*>(&hi))
+                     : "memory");
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k_lo >> 3) ^ (t & 7)) << 4) + (k_lo & 7) * 2),
+                     "h"(*reinterpret_cast<const unsigned short*>(&lo))
+                     : "memory");
       } else {
 #pragma unroll 1
         for (int c = 0; c < kDh / 32; ++c) {
@@ -677,7 +670,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float g_bf = bf16_round(has_tail ? g_tot * inv_l : 0.f);
       const int r = qb * 128 + t;
       const size_t orow = static_cast<size_t>(bank) * a.rows + r;
-      __nv_bfloat16* dst = a.out + orow * D + h * kDh;
+      // the merged rows are staged in the first vbar^T slot (free once the last P.V has
+      // completed): row t at 2 D bytes, its 16-byte chunks XOR-swizzled by t mod 8; each
+      // warp then stores its 32 half-rows as whole D-byte runs, 256 / D rows per instruction
+      const uint32_t stage = smem_u32(sV);
 #pragma unroll 1
       for (int c = 0; c < kDh / 32; ++c) {
         float ov[32], xv[32];
@@ -696,9 +692,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           w[e] = pack_bf16(res[0], res[1]);
         }
-        uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) st_stream_v4(d4 + q, make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]));
+        for (int q = 0; q < 4; ++q) {
+          const int j = (h * kDh + c * 32) / 8 + q;  // 16-byte chunk of the row
+          st_shared_v4(stage + t * (2 * D) + ((j ^ (t & 7)) << 4), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        }
+      }
+      __syncwarp();
+      {
+        constexpr int kHalfChunks = kDh / 8;      // 16-byte chunks of a half-row
+        constexpr int kRowsPer = 32 / kHalfChunks;
+        const int jj = h * kHalfChunks + lane % kHalfChunks;
+#pragma unroll 1
+        for (int i0 = 0; i0 < 32; i0 += kRowsPer) {
+          const int ti = q4 * 32 + i0 + lane / kHalfChunks;
+          uint32_t w0, w1, w2, w3;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                       : "r"(stage + ti * (2 * D) + ((jj ^ (ti & 7)) << 4)));
+          st_stream_v4(a.out + (static_cast<size_t>(bank) * a.rows + qb * 128 + ti) * D + jj * 8,
+                       make_uint4(w0, w1, w2, w3));
+        }
       }
       if (h == 0) {
         a.lse[orow] = lse;
@@ -739,7 +753,7 @@ int launch_coarse(const CoarseLaunch& L, cudaStream_t s) {
   const CoarseArgs& a = L.args;
   if (a.rows % 128 || a.nB_pad % kTileN || a.nB_pad > kMaxBlocks || a.rank < 0) return kErrShape;
   if (a.rows == 0) return kOk;
-  const bool fold = a.rank > 0 && a.rank + 2 <= 64 && a.rank + 2 <= L.D;
+  const bool fold = a.rank > 0 && a.rank + 4 <= 64 && a.rank + 4 <= L.D;
   if (L.D == 128) return fold ? launch_coarse_t<128, true>(L, s) : launch_coarse_t<128, false>(L, s);
   if (L.D == 64) return fold ? launch_coarse_t<64, true>(L, s) : launch_coarse_t<64, false>(L, s);
   return kErrShape;

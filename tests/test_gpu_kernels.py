@@ -362,11 +362,12 @@ def test_coarse_tail_bound_paths_vs_oracle(mode):
     _check_coarse_tail(128, 128 * 290 + 77, 50, True, None, mode=mode)
 
 
-@pytest.mark.parametrize("d,rank", [(128, 0), (64, 0), (128, 20), (64, 62), (128, 1)])
+@pytest.mark.parametrize("d,rank", [(128, 0), (64, 0), (128, 20), (64, 60), (64, 62), (128, 1)])
 def test_coarse_tail_ranks_vs_oracle(d, rank):
-    """The quadratic term over a folded variance (rank + 2 columns, one to four K-steps)
-    and over the full head dimension (rank 0: not folded), with 291 key blocks: three
-    tiles of block means through the operand rings, the last one mostly padding."""
+    """The quadratic term over a folded variance (rank + 4 columns, one to four K-steps;
+    rank 62 of 64 is past the fold and runs unfolded) and over the full head dimension
+    (rank 0: not folded), with 291 key blocks: three tiles of block means through the
+    operand rings, the last one mostly padding."""
     _check_coarse_tail(d, 128 * 290 + 77, 50, True, rank)
 
 
