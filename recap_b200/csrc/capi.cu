@@ -262,6 +262,7 @@ static int fmha_common(const void* q_reordered, const void* k_reordered, const v
   (void)g;
   int rc = kOk;
   const int S_pad = ((S + 127) / 128) * 128;
+  L->args.q = static_cast<const __nv_bfloat16*>(q_reordered);
   rc |= make_tmap_bf16(&L->tm_q, q_reordered, static_cast<uint64_t>(banks) * S_pad, D, 128);
   rc |= make_tmap_bf16(&L->tm_k, k_reordered, static_cast<uint64_t>(banks) * S_pad, D, 128);
   rc |= make_tmap_bf16(&L->tm_vt, v_transposed, static_cast<uint64_t>(banks) * D, S_pad, D);

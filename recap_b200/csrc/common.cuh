@@ -144,6 +144,13 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) from global memory into L2 (no shared memory, no
+// completion to wait for).  src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 // L2 policies: keep data that many CTAs re-read (a bank's K and V tiles) ahead of
 // streams read or written once (query tiles, epilogue inputs and outputs).
 __device__ __forceinline__ uint64_t l2_evict_last() {

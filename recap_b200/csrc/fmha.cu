@@ -40,6 +40,7 @@ namespace {
 
 constexpr int kThreads = 320;
 constexpr int kSoftmaxWarp0 = 2;
+constexpr int kNumSmsGuess = 148;  // B200: one CTA per SM
 constexpr int kMaxKeyBlocks = 2048;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by 2^8
 // Largest logit excess over the running max (log2 units) the bounded path accepts: every
@@ -94,10 +95,9 @@ struct Item {
   int bank, qa, qb;
 };
 
-__device__ __forceinline__ Item decode_item(const FmhaArgs& a) {
+__device__ __forceinline__ Item decode_item(const FmhaArgs& a, int b) {
   Item it;
   const int NB = a.NB;
-  int b = blockIdx.x;
   if (a.all_blocks) {
     const int per = (NB + 1) / 2;
     it.bank = b / per;
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const Item it = decode_item(args);
+  const Item it = decode_item(args, blockIdx.x);
   const int NB = args.NB;
   const bool has_b = it.qb >= 0;
   const bool dense_a = args.all_blocks || it.qa >= args.dense_start;
@@ -359,6 +359,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int a = 0; a < D / 64; ++a)
               tma_load_2d_hint(dst + a * 128 * 128, k == 0 ? &tm_go : &tm_det, bars.full + slot, a * 64, row0, stream);
             ++load_no;
+          }
+        }
+      }
+      // The CTA that starts when this one ends is about blockIdx.x + the number of SMs: put
+      // its Q tiles and partition rows into L2 now, so that its prologue does not wait on
+      // HBM (a hint: a wrong guess costs 64 KB of reads).
+      if (args.q != nullptr && !*abort_flag) {
+        const int nxt = blockIdx.x + kNumSmsGuess;
+        if (nxt < static_cast<int>(gridDim.x)) {
+          const Item in = decode_item(args, nxt);
+#pragma unroll
+          for (int y = 0; y < 2; ++y) {
+            const int qblock = y == 0 ? in.qa : in.qb;
+            if (qblock < 0) continue;
+            prefetch_l2_bulk(args.q + (static_cast<size_t>(in.bank) * args.S_pad + qblock * 128) * D, kTileBytes);
+            const bool dense_q = args.all_blocks || qblock >= args.dense_start;
+            if (!dense_q) {
+              // the whole 16-byte pieces inside the partition row
+              const uintptr_t lo = reinterpret_cast<uintptr_t>(args.partition +
+                                                               (static_cast<size_t>(in.bank) * args.nB + qblock) * args.nB);
+              const uintptr_t a16 = (lo + 15) & ~static_cast<uintptr_t>(15);
+              const uintptr_t e16 = (lo + args.dense_start) & ~static_cast<uintptr_t>(15);
+              if (e16 > a16) prefetch_l2_bulk(reinterpret_cast<const void*>(a16), static_cast<uint32_t>(e16 - a16));
+            }
           }
         }
       }

@@ -155,6 +155,7 @@ struct FmhaArgs {
   const float* ogl;        // [banks, rows] coarse LSE at the refresh
   const float* center;     // [banks]
   int tma_epilogue;        // 1: tm_go / tm_det describe go / det (epilogue 1 with video rows)
+  const __nv_bfloat16* q;  // [banks, S_pad, D] reordered Q (the tiles tm_q reads; L2 prefetch)
   int* status;
 };
 struct FmhaLaunch {
