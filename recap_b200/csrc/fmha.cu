@@ -225,73 +225,91 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- key-block lists: stage the two partition rows (independent loads), then
   // one warp splits them into blocks kept by both / by A only / by B only.
   const size_t part_bank = static_cast<size_t>(it.bank) * args.nB;
-  if (!dense_a) {
-    const uint8_t* p = args.partition + (part_bank + it.qa) * args.nB;
-    for (int j = threadIdx.x; j < args.dense_start; j += kThreads) row_a[j] = p[j];
-  }
-  if (has_b && !dense_b) {
-    const uint8_t* p = args.partition + (part_bank + it.qb) * args.nB;
-    for (int j = threadIdx.x; j < args.dense_start; j += kThreads) row_b[j] = p[j];
+  {
+    // all of this thread's byte loads first (one latency), then the stores
+    constexpr int kPer = (kMaxKeyBlocks + kThreads - 1) / kThreads;
+    const uint8_t* pa = dense_a ? nullptr : args.partition + (part_bank + it.qa) * args.nB;
+    const uint8_t* pb = (has_b && !dense_b) ? args.partition + (part_bank + it.qb) * args.nB : nullptr;
+    uint8_t va[kPer], vb[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int j = threadIdx.x + i * kThreads;
+      va[i] = (pa != nullptr && j < args.dense_start) ? pa[j] : 0;
+      vb[i] = (pb != nullptr && j < args.dense_start) ? pb[j] : 0;
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int j = threadIdx.x + i * kThreads;
+      if (j < args.dense_start) {
+        row_a[j] = va[i];
+        row_b[j] = vb[i];
+      }
+    }
   }
   __syncthreads();
   {
-    // Key-block lists by a block-wide compaction: warp w owns a contiguous range of
-    // 32-block chunks; pass 1 counts its blocks kept by both tiles / by A only / by B only,
-    // pass 2 writes them at offsets from the per-warp counts, so every category keeps
-    // ascending block order (shared blocks first in list_a, then A's own).
+    // Key-block lists by a block-wide compaction in one pass: thread q takes blocks
+    // 8q .. 8q + 7 (two 32-bit words of each staged row), counts its blocks kept by both
+    // tiles / by A only / by B only, and writes them at its exclusive prefix over the
+    // threads before it, so every category keeps ascending block order (shared blocks
+    // first in list_a, then A's own).  8 kThreads >= kMaxKeyBlocks.
+    static_assert(8 * kThreads >= kMaxKeyBlocks, "one compaction pass");
     constexpr int kWarps = kThreads / 32;
-    const int n_chunks = (NB + 31) / 32;
-    const int per = (n_chunks + kWarps - 1) / kWarps;
-    const int c0 = warp * per;
-    const int c1 = min(n_chunks, c0 + per);
-    const unsigned below = (1u << lane) - 1u;
-    auto masks = [&](int c, unsigned& ms, unsigned& ma, unsigned& mb) {
-      const int j = c * 32 + lane;
-      const bool in = j < NB;
-      const bool forced = j >= args.dense_start;
-      const bool ka = in && (dense_a || forced || row_a[j] != 0);
-      const bool kb = in && has_b && (dense_b || forced || row_b[j] != 0);
-      ms = __ballot_sync(0xffffffffu, ka && kb);
-      ma = __ballot_sync(0xffffffffu, ka && !kb);
-      mb = __ballot_sync(0xffffffffu, kb && !ka);
-    };
-    int cs = 0, ca = 0, cb = 0;
-    for (int c = c0; c < c1; ++c) {
-      unsigned ms, ma, mb;
-      masks(c, ms, ma, mb);
-      cs += __popc(ms);
-      ca += __popc(ma);
-      cb += __popc(mb);
-    }
-    if (lane == 0) {
-      counts[3 * warp] = cs;
-      counts[3 * warp + 1] = ca;
-      counts[3 * warp + 2] = cb;
-    }
-    __syncthreads();
-    int os = 0, oa = 0, ob = 0, n_shared = 0, ta = 0, tb = 0;
-    for (int w = 0; w < kWarps; ++w) {
-      const int ws = counts[3 * w], wa = counts[3 * w + 1], wb = counts[3 * w + 2];
-      n_shared += ws;
-      ta += wa;
-      tb += wb;
-      if (w < warp) {
-        os += ws;
-        oa += wa;
-        ob += wb;
+    const int q = threadIdx.x;
+    uint32_t bs = 0, ba = 0, bb = 0;  // bit e: block 8q + e in the category
+    if (8 * q < NB) {
+      const uint2 wa = reinterpret_cast<const uint2*>(row_a)[q];
+      const uint2 wb = reinterpret_cast<const uint2*>(row_b)[q];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = 8 * q + e;
+        const bool in = j < NB;
+        const bool forced = j >= args.dense_start;
+        const uint32_t va = ((e < 4 ? wa.x : wa.y) >> (8 * (e & 3))) & 0xffu;
+        const uint32_t vb = ((e < 4 ? wb.x : wb.y) >> (8 * (e & 3))) & 0xffu;
+        const bool ka = in && (dense_a || forced || va != 0);
+        const bool kb = in && has_b && (dense_b || forced || vb != 0);
+        bs |= (ka && kb) ? 1u << e : 0u;
+        ba |= (ka && !kb) ? 1u << e : 0u;
+        bb |= (kb && !ka) ? 1u << e : 0u;
       }
     }
-    oa += n_shared;
-    for (int c = c0; c < c1; ++c) {
-      unsigned ms, ma, mb;
-      masks(c, ms, ma, mb);
-      const uint16_t j = static_cast<uint16_t>(c * 32 + lane);
-      if ((ms >> lane) & 1u) list_a[os + __popc(ms & below)] = j;
-      if ((ma >> lane) & 1u) list_a[oa + __popc(ma & below)] = j;
-      if ((mb >> lane) & 1u) only_b[ob + __popc(mb & below)] = j;
-      os += __popc(ms);
-      oa += __popc(ma);
-      ob += __popc(mb);
+    // inclusive warp scans of the counts: (shared | A-only << 16) and B-only
+    const uint32_t m1 = __popc(bs) | (__popc(ba) << 16), m2 = __popc(bb);
+    uint32_t i1 = m1, i2 = m2;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t u1 = __shfl_up_sync(0xffffffffu, i1, o);
+      const uint32_t u2 = __shfl_up_sync(0xffffffffu, i2, o);
+      if (lane >= o) {
+        i1 += u1;
+        i2 += u2;
+      }
+    }
+    if (lane == 31) {
+      counts[2 * warp] = static_cast<int>(i1);
+      counts[2 * warp + 1] = static_cast<int>(i2);
+    }
+    __syncthreads();
+    uint32_t b1 = i1 - m1, b2 = i2 - m2, t1 = 0, t2 = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const uint32_t c1 = static_cast<uint32_t>(counts[2 * w]), c2 = static_cast<uint32_t>(counts[2 * w + 1]);
+      if (w < warp) {
+        b1 += c1;
+        b2 += c2;
+      }
+      t1 += c1;
+      t2 += c2;
+    }
+    const int n_shared = t1 & 0xffff, ta = t1 >> 16, tb = t2;
+    int os = b1 & 0xffff, oa = n_shared + (b1 >> 16), ob = b2;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint16_t j = static_cast<uint16_t>(8 * q + e);
+      if ((bs >> e) & 1u) list_a[os++] = j;
+      if ((ba >> e) & 1u) list_a[oa++] = j;
+      if ((bb >> e) & 1u) only_b[ob++] = j;
     }
     if (threadIdx.x == 0) {
       lens[0] = n_shared + ta;
