@@ -203,13 +203,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the largest |bf16(kbar_j)| of every tile of 128 block means
     const uint8_t* prow = a.partition + (static_cast<size_t>(bank) * nB + qb) * nB;
     const float* kmn = a.k_mean_norm ? a.k_mean_norm + static_cast<size_t>(bank) * nB : nullptr;
-    for (int base = 0; base < a.nB_pad; base += kThreads) {
+    // every load of this thread first (one latency), then the column terms
+    constexpr int kPer = (kMaxBlocks + kThreads - 1) / kThreads;
+    uint8_t pr[kPer];
+    float cl[kPer], kv[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int j = i * kThreads + threadIdx.x;
+      const bool in = j < nB;
+      pr[i] = in ? prow[j] : 1;
+      cl[i] = in ? a.counts_log[j] : 0.f;
+      kv[i] = (in && kmn != nullptr) ? kmn[j] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int base = i * kThreads;
+      if (base >= a.nB_pad) break;
       const int j = base + threadIdx.x;
-      float kn = 0.f;
-      if (j < a.nB_pad) {
-        colterm[j] = (j < nB && prow[j] == 0) ? a.counts_log[j] * kLog2e : -INFINITY;
-        if (kmn != nullptr && j < nB) kn = kmn[j];
-      }
+      float kn = kv[i];
+      if (j < a.nB_pad) colterm[j] = (j < nB && pr[i] == 0) ? cl[i] * kLog2e : -INFINITY;
       if (kmn != nullptr) {
         // one warp's 32 blocks lie in one tile (128 and kThreads are multiples of 32)
         for (int o = 16; o > 0; o >>= 1) kn = fmaxf(kn, __shfl_xor_sync(0xffffffffu, kn, o));
