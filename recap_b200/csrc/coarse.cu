@@ -452,10 +452,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(t_o + h * kDh + c * 32 + lane_base, v);
           tmem_wait_ld();
 #pragma unroll
+          for (int e = 0; e < 32; e += 2) bf16_round2(v[e], v[e + 1]);
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float s0 = v[e] * v[e], s1 = v[e + 1] * v[e + 1];
+            bf16_round2(s0, s1);
+            v[e] = s0;
+            v[e + 1] = s1;
+          }
+#pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int k = h * kDh + c * 32 + e;
-            const float xq = bf16_round(v[e]);
-            const float q2 = bf16_round(xq * xq);
+            const float q2 = v[e];
             if (k < rank) {
               const __nv_bfloat16 hb = __float2bfloat16_rn(q2);
               asm volatile("st.shared.b16 [%0], %1;" ::"r"(qsq_row + (((k >> 3) ^ (t & 7)) << 4) + (k & 7) * 2),
@@ -484,8 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float x0 = bf16_round(v[2 * e]);
-            const float x1 = bf16_round(v[2 * e + 1]);
+            float x0 = v[2 * e], x1 = v[2 * e + 1];
+            bf16_round2(x0, x1);
             pk[e] = pack_bf16(x0 * x0, x1 * x1);
           }
 #pragma unroll
@@ -695,14 +703,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          float res[2];
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const float o = has_tail ? bf16_round(ov[2 * e + i] * inv_l) : 0.f;
-            const float drift = bf16_round(scale * bf16_round(xv[2 * e + i]));
-            res[i] = o + bf16_round(g_bf * drift);
-          }
-          w[e] = pack_bf16(res[0], res[1]);
+          float o0 = ov[2 * e] * inv_l, o1 = ov[2 * e + 1] * inv_l;
+          bf16_round2(o0, o1);
+          if (!has_tail) o0 = o1 = 0.f;
+          float x0 = xv[2 * e], x1 = xv[2 * e + 1];
+          bf16_round2(x0, x1);
+          float d0 = scale * x0, d1 = scale * x1;
+          bf16_round2(d0, d1);
+          float g0 = g_bf * d0, g1 = g_bf * d1;
+          bf16_round2(g0, g1);
+          w[e] = pack_bf16(o0 + g0, o1 + g1);
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {

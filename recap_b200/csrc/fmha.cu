@@ -676,8 +676,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float2 gf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[e]));
               const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dw[e]));
               const int i0 = 8 * q + 2 * e;
-              const float oh0 = bf16_round(v[i0] * inv_l);
-              const float oh1 = bf16_round(v[i0 + 1] * inv_l);
+              float oh0 = v[i0] * inv_l, oh1 = v[i0 + 1] * inv_l;
+              bf16_round2(oh0, oh1);
               const float to0 = (gf.x * ms + (gf.x + df.x) * mc) * inv_td;
               const float to1 = (gf.y * ms + (gf.y + df.y) * mc) * inv_td;
               res[e] = pack_bf16((oh0 * wh + to0 * wt) * inv_den, (oh1 * wh + to1 * wt) * inv_den);
