@@ -57,8 +57,9 @@ struct GatherSmem {
   static constexpr int kK = kV + 128 * D * 2;
   static constexpr int kRed = kK + 128 * D * 2;              // [RPP][D] fp32
   static constexpr int kMean = kRed + 32 * D * 4;            // [D] fp32 key means
-  static constexpr int kRot = kMean + D * 4;                 // [128][kMaxRank] fp32
-  static constexpr int kStat = kRot + 128 * kMaxRank * 4;    // [2*kMaxRank + 1]
+  static constexpr int kRot = kMean + D * 4;                 // [2 halves][128][kMaxRank] fp32
+  static constexpr int kUs = kRot + 2 * 128 * kMaxRank * 4;  // [D][kMaxRank] leading basis columns
+  static constexpr int kStat = kUs + D * kMaxRank * 4;       // [2*kMaxRank + 1]
   static constexpr int kTotal = kStat + 64 * 4;
 };
 
@@ -74,6 +75,7 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
   float* red = reinterpret_cast<float*>(smem + L::kRed);
   float* kmean_s = reinterpret_cast<float*>(smem + L::kMean);
   float* rot = reinterpret_cast<float*>(smem + L::kRot);
+  float* us = reinterpret_cast<float*>(smem + L::kUs);
   float* stat = reinterpret_cast<float*>(smem + L::kStat);
 
   const int blk = blockIdx.x;
@@ -86,6 +88,13 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
   const int row0 = blk * 128;
   const int video_rows = min(128, a.n_video - row0);  // <= 0 for text-only blocks
   const bool need_k_tile = (a.kct != nullptr || a.variance != nullptr) && video_rows > 0;
+
+  // The variance pass's leading basis columns U[d][0 .. rank), staged now: their loads
+  // overlap the gathers (us is read only after the later barriers).
+  if (a.variance != nullptr && blk < a.nB && video_rows > 0 && tid < D) {
+    const float* U = a.basis + (static_cast<size_t>(bank) * D + tid) * D;
+    for (int c = 0; c < a.rank; ++c) us[tid * kMaxRank + c] = U[c];
+  }
 
   // Native rows of this thread's PASSES rows, then each tensor's PASSES row chunks in
   // one burst of independent loads (two tensors in flight): the pass is bound by the
@@ -246,58 +255,62 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
 
   if (a.variance != nullptr && blk < a.nB && video_rows > 0) {
     const int rank = a.rank;
-    const float* U = a.basis + static_cast<size_t>(bank) * D * D;
-    // leading basis columns, staged as us[c][d] (read as broadcasts below)
-    float* us = red;  // the pooling scratch is free here: [kMaxRank][D] fits in [32][D]
-    for (int idx = tid; idx < rank * D; idx += kThreads) {
-      const int c = idx / D;
-      const int d = idx % D;
-      us[c * D + d] = U[d * D + c];
-    }
-    __syncthreads();
-    // rotated values of the leading columns, one key row per thread:
-    // rot[r][c] = sum_d k[r][d] U[d][c]
-    if (tid < 128) {
-      const int r = tid;
+    // rotated values of the leading columns: rot[r][c] = sum_d k[r][d] U[d][c], thread
+    // (half, r) summing its half of the head dimension; and the trace of the block
+    // covariance, sum_d sum_r (k[r][d] - m_d)^2, thread (half, d) over its half of the rows
+    const int r = tid & 127;
+    const int half = tid >> 7;
+    {
       float acc[kMaxRank];
 #pragma unroll
       for (int c = 0; c < kMaxRank; ++c) acc[c] = 0.f;
       if (r < video_rows) {
-#pragma unroll 4
-        for (int j = 0; j < D / 8; ++j) {
+#pragma unroll 2
+        for (int j = half * (CPR / 2); j < (half + 1) * (CPR / 2); ++j) {
           const uint4 w = *reinterpret_cast<const uint4*>(ktile + stage_off<D>(r, j));
           const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-          float x[8];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = __bfloat1622float2(h[e]);
-            x[2 * e] = f.x;
-            x[2 * e + 1] = f.y;
-          }
+            const int d = j * 8 + 2 * e;
+            const float4 u0a = *reinterpret_cast<const float4*>(us + d * kMaxRank);
+            const float4 u0b = *reinterpret_cast<const float4*>(us + d * kMaxRank + 4);
+            const float4 u1a = *reinterpret_cast<const float4*>(us + (d + 1) * kMaxRank);
+            const float4 u1b = *reinterpret_cast<const float4*>(us + (d + 1) * kMaxRank + 4);
+            const float ua[8] = {u0a.x, u0a.y, u0a.z, u0a.w, u0b.x, u0b.y, u0b.z, u0b.w};
+            const float ub[8] = {u1a.x, u1a.y, u1a.z, u1a.w, u1b.x, u1b.y, u1b.z, u1b.w};
 #pragma unroll
-          for (int c = 0; c < kMaxRank; ++c) {
-            if (c < rank) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) acc[c] = fmaf(x[e], us[c * D + j * 8 + e], acc[c]);
-            }
+            for (int c = 0; c < kMaxRank; ++c)
+              if (c < rank) acc[c] = fmaf(f.y, ub[c], fmaf(f.x, ua[c], acc[c]));
           }
         }
       }
 #pragma unroll
-      for (int c = 0; c < kMaxRank; ++c) rot[r * kMaxRank + c] = acc[c];
+      for (int c = 0; c < kMaxRank; ++c) rot[(half * 128 + r) * kMaxRank + c] = acc[c];
     }
-    __syncthreads();  // us (in red) is read before red takes the trace partial sums
-    // per-dimension squared deviations for the trace of the block covariance
     float tr = 0.f;
-    if (tid < D) {
-      const float m = kmean_s[tid];
-      for (int r = 0; r < video_rows; ++r) {
-        const float x = __bfloat162float(stage_elem<D>(ktile, r, tid)) - m;
-        tr = fmaf(x, x, tr);
+    {
+      const int d = tid & (D - 1);
+      const int rows_per = 128 * D / kThreads;  // rows per thread: D threads per row
+      const int part = tid / D;
+      const float m = kmean_s[d];
+      float t4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int i = 0; i < rows_per; ++i) {
+        const int rr = part * rows_per + i;
+        const float x = rr < video_rows ? __bfloat162float(stage_elem<D>(ktile, rr, d)) - m : 0.f;
+        t4[i & 3] = fmaf(x, x, t4[i & 3]);
       }
+      tr = (t4[0] + t4[1]) + (t4[2] + t4[3]);
     }
     for (int o = 16; o > 0; o >>= 1) tr += __shfl_xor_sync(0xffffffffu, tr, o);
-    if ((tid & 31) == 0 && tid < D) red[tid >> 5] = tr;
+    __syncthreads();  // red (the pooling scratch) is free for the trace partial sums
+    if ((tid & 31) == 0) red[tid >> 5] = tr;
+    // combine the two halves of rot
+    if (tid < 128) {
+#pragma unroll
+      for (int c = 0; c < kMaxRank; ++c) rot[tid * kMaxRank + c] += rot[(128 + tid) * kMaxRank + c];
+    }
     __syncthreads();
     if ((tid >> 5) < rank) {
       // two-pass population variance of column c of K U, one warp per column
@@ -322,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
         v = stat[tid];
       } else {
         float total = 0.f;
-        for (int q = 0; q < D / 32; ++q) total += red[q];
+        for (int q = 0; q < kThreads / 32; ++q) total += red[q];
         total /= static_cast<float>(video_rows);
         float lead = 0.f;
         for (int c = 0; c < rank; ++c) lead += stat[c];
