@@ -41,6 +41,22 @@ __device__ __forceinline__ void add8(float (&acc)[8], const uint4& w) {
 // chunk ^ ((r / 8) mod (D / 8)).  Lanes that read eight consecutive rows of one column
 // (the transposed stores) then see distinct chunks; lanes that read a row see a
 // permutation of its chunks.
+// Four 8x8 bf16 matrices from shared memory, each lane addressing one 16-byte row.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// d += a * b for one 16x8x16 bf16 tile with fp32 accumulation (warp-wide).
+__device__ __forceinline__ void mma_m16n8k16_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 template <int D>
 __device__ __forceinline__ uint32_t stage_off(int r, int chunk) {
   constexpr int CPR = D / 8;
@@ -57,9 +73,10 @@ struct GatherSmem {
   static constexpr int kK = kV + 128 * D * 2;
   static constexpr int kRed = kK + 128 * D * 2;              // [RPP][D] fp32
   static constexpr int kMean = kRed + 32 * D * 4;            // [D] fp32 key means
-  static constexpr int kRot = kMean + D * 4;                 // [2 halves][128][kMaxRank] fp32
-  static constexpr int kUs = kRot + 2 * 128 * kMaxRank * 4;  // [D][kMaxRank] leading basis columns
-  static constexpr int kStat = kUs + D * kMaxRank * 4;       // [2*kMaxRank + 1]
+  // leading basis columns as mma.m16n8k16 B fragments, U = hi + mid + lo in bf16:
+  // [part][k-step][lane][4] bf16
+  static constexpr int kUf = kMean + D * 4;
+  static constexpr int kStat = kUf + 3 * (D / 16) * 32 * 8;  // [2*kMaxRank + 1]
   static constexpr int kTotal = kStat + 64 * 4;
 };
 
@@ -74,8 +91,7 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
   uint8_t* ktile = smem + L::kK;
   float* red = reinterpret_cast<float*>(smem + L::kRed);
   float* kmean_s = reinterpret_cast<float*>(smem + L::kMean);
-  float* rot = reinterpret_cast<float*>(smem + L::kRot);
-  float* us = reinterpret_cast<float*>(smem + L::kUs);
+  __nv_bfloat16* ufrag = reinterpret_cast<__nv_bfloat16*>(smem + L::kUf);
   float* stat = reinterpret_cast<float*>(smem + L::kStat);
 
   const int blk = blockIdx.x;
@@ -89,11 +105,30 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
   const int video_rows = min(128, a.n_video - row0);  // <= 0 for text-only blocks
   const bool need_k_tile = (a.kct != nullptr || a.variance != nullptr) && video_rows > 0;
 
-  // The variance pass's leading basis columns U[d][0 .. rank), staged now: their loads
-  // overlap the gathers (us is read only after the later barriers).
+  // The variance pass's leading basis columns U[d][0 .. rank) (zero past the rank), staged
+  // now so that their loads overlap the gathers (ufrag is read only after later barriers).
+  // Each value is split into three bf16 parts, hi + mid + lo, whose sum is the fp32 value
+  // to within 2^-24 relative: the tensor-core products of bf16 keys with each part are
+  // exact, so the rotation keeps fp32 accuracy.  Element (d, c) goes where lane 4c + t of
+  // an m16n8k16 B fragment holds it: k-step d / 16, t = (d % 8) / 2, register (d % 16) / 8.
   if (a.variance != nullptr && blk < a.nB && video_rows > 0 && tid < D) {
     const float* U = a.basis + (static_cast<size_t>(bank) * D + tid) * D;
-    for (int c = 0; c < a.rank; ++c) us[tid * kMaxRank + c] = U[c];
+    const int ks = tid >> 4;
+    const int w16 = tid & 15;
+    const int slot = (w16 >> 3) * 2 + (w16 & 1);
+    const int t = (w16 & 7) >> 1;
+#pragma unroll
+    for (int c = 0; c < kMaxRank; ++c) {
+      const float u = c < a.rank ? U[c] : 0.f;
+      const __nv_bfloat16 hi = __float2bfloat16_rn(u);
+      const float r1 = u - __bfloat162float(hi);
+      const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+      const int lane_c = c * 4 + t;
+      ufrag[((0 * (D / 16) + ks) * 32 + lane_c) * 4 + slot] = hi;
+      ufrag[((1 * (D / 16) + ks) * 32 + lane_c) * 4 + slot] = mid;
+      ufrag[((2 * (D / 16) + ks) * 32 + lane_c) * 4 + slot] = lo;
+    }
   }
 
   // Native rows of this thread's PASSES rows, then each tensor's PASSES row chunks in
@@ -255,90 +290,119 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
 
   if (a.variance != nullptr && blk < a.nB && video_rows > 0) {
     const int rank = a.rank;
-    // rotated values of the leading columns: rot[r][c] = sum_d k[r][d] U[d][c], thread
-    // (half, r) summing its half of the head dimension; and the trace of the block
-    // covariance, sum_d sum_r (k[r][d] - m_d)^2, thread (half, d) over its half of the rows
-    const int r = tid & 127;
-    const int half = tid >> 7;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    // Rotated values of the leading columns, rot[r][c] = sum_d k[r][d] U[d][c], on the tensor
+    // cores: warp w takes the sixteen rows 8m + w (m = 0 .. 15; the stride makes the eight
+    // rows of each ldmatrix phase fall in eight different swizzle chunks, so the loads are
+    // free of bank conflicts) and one m16n8k16 MMA per k-step and part of U.  Thread (g, t)
+    // ends with rows 8g + w and 8(g + 8) + w, columns 2t and 2t + 1.
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     {
-      float acc[kMaxRank];
+      const int mrow = ((lane >> 3) & 1) * 8 + (lane & 7);  // ldmatrix row of this lane's address
+      const int kc = lane >> 4;                             // which 8-column half of the k-step
+      const uint2* bf = reinterpret_cast<const uint2*>(ufrag);
 #pragma unroll
-      for (int c = 0; c < kMaxRank; ++c) acc[c] = 0.f;
-      if (r < video_rows) {
-#pragma unroll 2
-        for (int j = half * (CPR / 2); j < (half + 1) * (CPR / 2); ++j) {
-          const uint4 w = *reinterpret_cast<const uint4*>(ktile + stage_off<D>(r, j));
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t af[4];
+        ldmatrix_x4(af, smem_u32(ktile + stage_off<D>(8 * mrow + warp, 2 * ks + kc)));
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h[e]);
-            const int d = j * 8 + 2 * e;
-            const float4 u0a = *reinterpret_cast<const float4*>(us + d * kMaxRank);
-            const float4 u0b = *reinterpret_cast<const float4*>(us + d * kMaxRank + 4);
-            const float4 u1a = *reinterpret_cast<const float4*>(us + (d + 1) * kMaxRank);
-            const float4 u1b = *reinterpret_cast<const float4*>(us + (d + 1) * kMaxRank + 4);
-            const float ua[8] = {u0a.x, u0a.y, u0a.z, u0a.w, u0b.x, u0b.y, u0b.z, u0b.w};
-            const float ub[8] = {u1a.x, u1a.y, u1a.z, u1a.w, u1b.x, u1b.y, u1b.z, u1b.w};
-#pragma unroll
-            for (int c = 0; c < kMaxRank; ++c)
-              if (c < rank) acc[c] = fmaf(f.y, ub[c], fmaf(f.x, ua[c], acc[c]));
-          }
+        for (int part = 0; part < 3; ++part) {
+          const uint2 b = bf[(part * (D / 16) + ks) * 32 + lane];
+          mma_m16n8k16_bf16(acc, af, b.x, b.y);
         }
       }
-#pragma unroll
-      for (int c = 0; c < kMaxRank; ++c) rot[(half * 128 + r) * kMaxRank + c] = acc[c];
     }
-    float tr = 0.f;
+    const int g = lane >> 2;
+    const int t = lane & 3;
+    const bool v0 = 8 * g + warp < video_rows;
+    const bool v1 = 8 * (g + 8) + warp < video_rows;
+    // The trace of the block covariance, sum_d sum_r (k[r][d] - m_d)^2: thread (part, pair)
+    // takes dimensions 2 pair and 2 pair + 1 over its share of the rows.
+    float tr;
     {
-      const int d = tid & (D - 1);
-      const int rows_per = 128 * D / kThreads;  // rows per thread: D threads per row
-      const int part = tid / D;
-      const float m = kmean_s[d];
-      float t4[4] = {0.f, 0.f, 0.f, 0.f};
+      constexpr int kPairs = D / 2;
+      constexpr int kParts = kThreads / kPairs;
+      constexpr int kRowsPer = 128 / kParts;
+      const int pr = tid % kPairs;
+      const int part = tid / kPairs;
+      const float m0 = kmean_s[2 * pr];
+      const float m1 = kmean_s[2 * pr + 1];
+      const int r0 = part * kRowsPer;
+      const int r1 = min(r0 + kRowsPer, video_rows);
+      float s0 = 0.f, s1 = 0.f;
 #pragma unroll 4
-      for (int i = 0; i < rows_per; ++i) {
-        const int rr = part * rows_per + i;
-        const float x = rr < video_rows ? __bfloat162float(stage_elem<D>(ktile, rr, d)) - m : 0.f;
-        t4[i & 3] = fmaf(x, x, t4[i & 3]);
+      for (int rr = r0; rr < r1; ++rr) {
+        const float2 f = __bfloat1622float2(
+            *reinterpret_cast<const __nv_bfloat162*>(ktile + stage_off<D>(rr, pr >> 2) + (pr & 3) * 4));
+        const float x0 = f.x - m0;
+        const float x1 = f.y - m1;
+        s0 = fmaf(x0, x0, s0);
+        s1 = fmaf(x1, x1, s1);
       }
-      tr = (t4[0] + t4[1]) + (t4[2] + t4[3]);
+      tr = s0 + s1;
     }
     for (int o = 16; o > 0; o >>= 1) tr += __shfl_xor_sync(0xffffffffu, tr, o);
-    __syncthreads();  // red (the pooling scratch) is free for the trace partial sums
-    if ((tid & 31) == 0) red[tid >> 5] = tr;
-    // combine the two halves of rot
-    if (tid < 128) {
-#pragma unroll
-      for (int c = 0; c < kMaxRank; ++c) rot[tid * kMaxRank + c] += rot[(128 + tid) * kMaxRank + c];
+    // Two-pass population variances of the rotated columns: column sums over the video rows
+    // (lanes of equal t, then the eight warps), the means, then the squared deviations.
+    float* colsum = red + 64;   // [8 warps][kMaxRank]; red (the pooling scratch) is free since the
+                                // barrier before the transposed stores
+    float* colsq = red + 128;   // [8 warps][kMaxRank]
+    float cs0 = (v0 ? acc[0] : 0.f) + (v1 ? acc[2] : 0.f);
+    float cs1 = (v0 ? acc[1] : 0.f) + (v1 ? acc[3] : 0.f);
+    for (int o = 4; o < 32; o <<= 1) {
+      cs0 += __shfl_xor_sync(0xffffffffu, cs0, o);
+      cs1 += __shfl_xor_sync(0xffffffffu, cs1, o);
+    }
+    if (lane == 0) red[warp] = tr;
+    if (lane < 4) {
+      colsum[warp * kMaxRank + 2 * t] = cs0;
+      colsum[warp * kMaxRank + 2 * t + 1] = cs1;
     }
     __syncthreads();
-    if ((tid >> 5) < rank) {
-      // two-pass population variance of column c of K U, one warp per column
-      const int c = tid >> 5;
-      const int lane = tid & 31;
-      float sum = 0.f;
-      for (int r = lane; r < video_rows; r += 32) sum += rot[r * kMaxRank + c];
-      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      const float m = sum / static_cast<float>(video_rows);
-      float ss = 0.f;
-      for (int r = lane; r < video_rows; r += 32) {
-        const float x = rot[r * kMaxRank + c] - m;
-        ss = fmaf(x, x, ss);
-      }
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) stat[c] = fmaxf(ss / static_cast<float>(video_rows), 0.f);
+    const float inv_n = 1.f / static_cast<float>(video_rows);
+    float mc0 = 0.f, mc1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) {
+      mc0 += colsum[w * kMaxRank + 2 * t];
+      mc1 += colsum[w * kMaxRank + 2 * t + 1];
+    }
+    mc0 *= inv_n;
+    mc1 *= inv_n;
+    float q0 = 0.f, q1 = 0.f;
+    if (v0) {
+      const float x0 = acc[0] - mc0, x1 = acc[1] - mc1;
+      q0 = x0 * x0;
+      q1 = x1 * x1;
+    }
+    if (v1) {
+      const float x0 = acc[2] - mc0, x1 = acc[3] - mc1;
+      q0 = fmaf(x0, x0, q0);
+      q1 = fmaf(x1, x1, q1);
+    }
+    for (int o = 4; o < 32; o <<= 1) {
+      q0 += __shfl_xor_sync(0xffffffffu, q0, o);
+      q1 += __shfl_xor_sync(0xffffffffu, q1, o);
+    }
+    if (lane < 4) {
+      colsq[warp * kMaxRank + 2 * t] = q0;
+      colsq[warp * kMaxRank + 2 * t + 1] = q1;
     }
     __syncthreads();
     if (tid < D) {
-      float v;
-      if (tid < rank) {
-        v = stat[tid];
-      } else {
+      float lead = 0.f;
+      float v = 0.f;
+      for (int c = 0; c < rank; ++c) {
+        float q = 0.f;
+        for (int w = 0; w < kThreads / 32; ++w) q += colsq[w * kMaxRank + c];
+        q = fmaxf(q * inv_n, 0.f);
+        lead += q;
+        if (c == tid) v = q;
+      }
+      if (tid >= rank) {
         float total = 0.f;
-        for (int q = 0; q < kThreads / 32; ++q) total += red[q];
-        total /= static_cast<float>(video_rows);
-        float lead = 0.f;
-        for (int c = 0; c < rank; ++c) lead += stat[c];
+        for (int w = 0; w < kThreads / 32; ++w) total += red[w];
+        total *= inv_n;
         v = fmaxf(total - lead, 0.f) / static_cast<float>(D - rank);
       }
       a.variance[(static_cast<size_t>(bank) * a.nB + blk) * D + tid] = v;
