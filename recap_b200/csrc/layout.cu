@@ -48,6 +48,14 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
                : "r"(addr));
 }
 
+// The same, each matrix transposed on the way (thread i receives column i / 4, rows
+// 2 (i % 4) and 2 (i % 4) + 1).
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
 // d += a * b for one 16x8x16 bf16 tile with fp32 accumulation (warp-wide).
 __device__ __forceinline__ void mma_m16n8k16_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -245,45 +253,49 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
   }
 
   __syncthreads();  // the staged V and K tiles are complete before anyone reads them back
-  // Transposed stores (V^T and the centred K^T): for each head dimension d this block
-  // owns 128 contiguous bf16 (256 bytes) of row d.  A half-warp writes one such row, each
-  // lane 8 consecutive tokens (16 bytes); a warp covers two dimensions per step.
+  // Transposed stores (V^T and the centred K^T): for each head dimension d this block owns
+  // 128 contiguous bf16 of row d.  A warp takes a tile of 32 tokens x 8 dimensions with one
+  // transposing ldmatrix: lane (j, q) addresses token 8(q/2) + 2j + q%2 of the tile, so that
+  // thread (dl, tq) receives dimension dl of tokens 8tq .. 8tq + 7 in order, one 16-byte
+  // store; a warp instruction writes eight 64-byte runs.
   {
     const int lane = tid & 31;
-    const int g = lane & 15;   // tokens 8g .. 8g + 7
-    const int dd = lane >> 4;  // which of the warp's two dimensions
+    const int warp = tid >> 5;
     constexpr int kWarps = kThreads / 32;
+    constexpr int kTiles = 4 * (D / 8);  // 4 token groups x D/8 dimension blocks
+    const int tok_in = 8 * ((lane & 7) >> 1) + 2 * (lane >> 3) + (lane & 1);
+    const int dl = lane >> 2;
+    const int tq = lane & 3;
     if (a.vt != nullptr && a.src[2] != nullptr) {
-      for (int d0 = 2 * (tid >> 5); d0 < D; d0 += 2 * kWarps) {
-        const int d = d0 + dd;
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const __nv_bfloat16 lo = stage_elem<D>(vtile, 8 * g + 2 * e, d);
-          const __nv_bfloat16 hi = stage_elem<D>(vtile, 8 * g + 2 * e + 1, d);
-          w[e] = static_cast<uint32_t>(__bfloat16_as_ushort(lo)) |
-                 (static_cast<uint32_t>(__bfloat16_as_ushort(hi)) << 16);
-        }
-        *reinterpret_cast<uint4*>(a.vt + (static_cast<size_t>(bank) * D + d) * a.S_pad + row0 + 8 * g) =
-            make_uint4(w[0], w[1], w[2], w[3]);
+      for (int tile = warp; tile < kTiles; tile += kWarps) {
+        const int tg = tile & 3;
+        const int db = tile >> 2;
+        uint32_t r[4];
+        ldmatrix_x4_trans(r, smem_u32(vtile + stage_off<D>(32 * tg + tok_in, db)));
+        *reinterpret_cast<uint4*>(a.vt + (static_cast<size_t>(bank) * D + 8 * db + dl) * a.S_pad + row0 + 32 * tg +
+                                  8 * tq) = make_uint4(r[0], r[1], r[2], r[3]);
       }
     }
     if (a.kct != nullptr) {
       // centred video keys, bf16; zero outside the video tokens
-      for (int d0 = 2 * (tid >> 5); d0 < D; d0 += 2 * kWarps) {
-        const int d = d0 + dd;
+      for (int tile = warp; tile < kTiles; tile += kWarps) {
+        const int tg = tile & 3;
+        const int db = tile >> 2;
+        const int d = 8 * db + dl;
         const float m = video_rows > 0 ? kmean_s[d] : 0.f;
-        uint32_t w[4];
+        uint32_t r[4];
+        ldmatrix_x4_trans(r, smem_u32(ktile + stage_off<D>(32 * tg + tok_in, db)));
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int r0 = 8 * g + 2 * e;
-          const float x0 = r0 < video_rows ? __bfloat162float(stage_elem<D>(ktile, r0, d)) - m : 0.f;
-          const float x1 = r0 + 1 < video_rows ? __bfloat162float(stage_elem<D>(ktile, r0 + 1, d)) - m : 0.f;
+          const int t0 = 32 * tg + 8 * tq + 2 * e;
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r[e]));
+          const float x0 = t0 < video_rows ? f.x - m : 0.f;
+          const float x1 = t0 + 1 < video_rows ? f.y - m : 0.f;
           const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+          r[e] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        *reinterpret_cast<uint4*>(a.kct + (static_cast<size_t>(bank) * D + d) * a.S_pad + row0 + 8 * g) =
-            make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(a.kct + (static_cast<size_t>(bank) * D + d) * a.S_pad + row0 + 32 * tg + 8 * tq) =
+            make_uint4(r[0], r[1], r[2], r[3]);
       }
     }
   }
