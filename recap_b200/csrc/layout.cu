@@ -37,10 +37,6 @@ __device__ __forceinline__ void add8(float (&acc)[8], const uint4& w) {
   }
 }
 
-// Staged 128 x D bf16 tiles: rows of D * 2 bytes, the 16-byte chunks of row r stored at
-// chunk ^ ((r / 8) mod (D / 8)).  Lanes that read eight consecutive rows of one column
-// (the transposed stores) then see distinct chunks; lanes that read a row see a
-// permutation of its chunks.
 // Four 8x8 bf16 matrices from shared memory, each lane addressing one 16-byte row.
 __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -65,6 +61,9 @@ __device__ __forceinline__ void mma_m16n8k16_bf16(float (&d)[4], const uint32_t 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Staged 128 x D bf16 tiles: rows of D * 2 bytes, the 16-byte chunks of row r stored at
+// chunk ^ ((r / 8) mod (D / 8)).  One chunk of eight rows spaced eight apart lies in eight
+// different bank groups, and lanes that read a row see a permutation of its chunks.
 template <int D>
 __device__ __forceinline__ uint32_t stage_off(int r, int chunk) {
   constexpr int CPR = D / 8;
