@@ -348,6 +348,29 @@ def test_closure_statistics_vs_oracle(d, nv, text, text_first):
 
 
 @pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("rank", [1, 3, 8, 20])
+def test_gather_folded_variance_ranks(d, rank):
+    """The layout pass's rank-folded variances (second call, basis known) at every rank
+    its tensor-core rotation takes (1 .. 8, zero columns past the rank) and one above,
+    which goes to the per-column kernel; a partial last video block (700 tokens)."""
+    nv, text = 700, 50
+    lay = _layout(nv, text, True)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=11)
+    sa, inp = _run_gather(lay, q, k, v, q_mean=False, closure_rank=rank)
+    ctx = sa.coarse_tail_context(inp, 1 / math.sqrt(d))
+    inp2 = sa.prepare(q, k, v, q_mean=False)
+    ctx2 = sa.coarse_tail_context(inp2, 1 / math.sqrt(d))
+    torch.cuda.synchronize()
+    from recap_b200 import _lib as lib
+
+    assert (inp2.variance is not None) == (rank <= lib.load().recap_gather_max_rank())
+    k_r = inp.k[:, : inp.shapes.S].float().cpu()
+    var = orc.fold_rank(orc.rotated_variance(k_r, ctx["basis"].cpu(), nv), rank)
+    got = ctx2["variance"].cpu()
+    assert torch.allclose(got, var, atol=1e-4, rtol=2e-3), (got - var).abs().max()
+
+
+@pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("nv,text,text_first", [(2048, 0, False), (700, 50, True)])
 def test_coarse_tail_vs_oracle(d, nv, text, text_first):
     _check_coarse_tail(d, nv, text, text_first, None)
