@@ -567,9 +567,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) {
             const int e = 4 * e4 + i;
             const float quad = v2[e];
-            const bool gt = quad <= gate_max;
-            gm |= gt ? (1u << e) : 0u;
-            x[c * 32 + e] = fmaf(quad, gt ? h_l2 : 0.f, fmaf(v1[e], s_l2, cts[i]));
+            // the gate as a branch: the compiler predicates the gated product and the
+            // mask bit (two integer-pipe instructions per element where a select of the
+            // factor and of the bit took four; that pipe bounds this loop)
+            const float base = fmaf(v1[e], s_l2, cts[i]);
+            float xg = base;
+            if (quad <= gate_max) {
+              xg = fmaf(quad, h_l2, base);
+              gm |= 1u << e;
+            }
+            x[c * 32 + e] = xg;
           }
         }
         // opaque copy: the exponential phase then tests these packed bits instead of the
