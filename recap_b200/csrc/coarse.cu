@@ -643,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const float neg_m = m_run == -INFINITY ? 0.f : -m_run;  // exp2(-inf + 0) = 0
-      float ls[4] = {0.f, 0.f, 0.f, 0.f}, gs[2] = {0.f, 0.f};
+      float ls[4] = {0.f, 0.f, 0.f, 0.f}, gs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
@@ -660,9 +660,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             p1 = fast_exp2(y1);
           }
           add2(ls[(i & 1) * 2], ls[(i & 1) * 2 + 1], p0, p1);
-          const float g0 = ((gate[c] >> e0) & 1u) ? p0 : 0.f;
-          const float g1 = ((gate[c] >> e1) & 1u) ? p1 : 0.f;
-          add2(gs[0], gs[1], g0, g1);
+          // gated mass: predicated adds into four partial sums (short dependency chains)
+          if ((gate[c] >> e0) & 1u) gs[(i & 1) * 2] += p0;
+          if ((gate[c] >> e1) & 1u) gs[(i & 1) * 2 + 1] += p1;
           pk[i] = pack_bf16(p0, p1);
         }
         // P of blocks 64h + 32c .. + 31 (two per column), in this half's own S1 columns
@@ -673,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bars.pfull);
       l_run = l_run * alpha + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
-      g_run = g_run * alpha + (gs[0] + gs[1]);
+      g_run = g_run * alpha + ((gs[0] + gs[1]) + (gs[2] + gs[3]));
     }
     // combine the halves' row sums
     float l_tot = l_run, g_tot = g_run;
