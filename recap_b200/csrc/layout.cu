@@ -52,6 +52,14 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t add
                : "r"(addr));
 }
 
+// 16-byte asynchronous copy from global to shared memory through L2 only; src_bytes = 0
+// writes sixteen zero bytes and reads nothing.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // d += a * b for one 16x8x16 bf16 tile with fp32 accumulation (warp-wide).
 __device__ __forceinline__ void mma_m16n8k16_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -173,12 +181,8 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
       const uint4 val = v[p];
       if (t == 0 && a.qr) {
         *reinterpret_cast<uint4*>(a.qr + (static_cast<size_t>(bank) * a.S_pad + r) * D + ch * 8) = val;
-      } else if (t == 1) {
-        if (a.kr)
-          *reinterpret_cast<uint4*>(a.kr + (static_cast<size_t>(bank) * a.S_pad + r) * D + ch * 8) = val;
-        if (need_k_tile) *reinterpret_cast<uint4*>(ktile + stage_off<D>(rl, ch)) = val;
-      } else if (t == 2) {
-        *reinterpret_cast<uint4*>(vtile + stage_off<D>(rl, ch)) = val;
+      } else if (t == 1 && a.kr) {
+        *reinterpret_cast<uint4*>(a.kr + (static_cast<size_t>(bank) * a.S_pad + r) * D + ch * 8) = val;
       }
       if (rl < video_rows) add8(acc, val);
       if (t == 1 && a.k_norm_max) {
@@ -230,12 +234,36 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
     }
   };
   {
-    uint4 va[PASSES], vb[PASSES];
+    // K and V go straight into their staged tiles by asynchronous copies (no registers),
+    // so the loads of all three tensors are in flight at once; Q comes to registers and
+    // is stored from there.  K and V are read back from shared memory for their stores,
+    // pools and norms.
+    auto copy_rows = [&](int t, uint8_t* tile) {
+      const __nv_bfloat16* src = a.src[t];
+      if (src == nullptr) return;
+      const __nv_bfloat16* base = src + bi * a.stride_b[t] + hi * a.stride_h[t] + ch * 8;
+#pragma unroll
+      for (int p = 0; p < PASSES; ++p) {
+        const bool in = nat[p] >= 0;
+        cp_async16(smem_u32(tile + stage_off<D>(p * RPP + rsub, ch)),
+                   in ? base + static_cast<int64_t>(nat[p]) * a.stride_s[t] : base, in ? 16u : 0u);
+      }
+    };
+    auto read_rows = [&](const uint8_t* tile, uint4 (&v)[PASSES]) {
+#pragma unroll
+      for (int p = 0; p < PASSES; ++p) v[p] = *reinterpret_cast<const uint4*>(tile + stage_off<D>(p * RPP + rsub, ch));
+    };
+    copy_rows(1, ktile);
+    copy_rows(2, vtile);
+    cp_async_commit();
+    uint4 va[PASSES];
     load_rows(0, va);
-    load_rows(1, vb);
     process(0, va);
-    load_rows(2, va);
-    process(1, vb);
+    cp_async_wait_all();
+    __syncthreads();  // every thread's copies have landed
+    read_rows(ktile, va);
+    process(1, va);
+    read_rows(vtile, va);
     process(2, va);
   }
   if (a.k_norm_max) {
