@@ -84,8 +84,8 @@ struct CoarseSmem {
   static constexpr int kSums = kXchg + 2 * 2 * 128 * 4;  // (l, g) per half [2][2][128], then T partials [128]
   static constexpr int kBars = kSums + (2 * 2 * 128 + 128) * 4;
   // pro_full, pro_mma, qsq_ready, kw_full[2], kw_empty[2], v_full[2], v_empty[2],
-  // s1full[2], s2full, s2free, pfull, ofull, c_full, xfull, done, xsum, tpart, xchg[2 slots][4 quarters]
-  static constexpr int kNumBars = 3 + 8 + 2 + 7 + 2 + 8;
+  // s1full[2], s2full, s2free, pfull, ofull, c_full, xfull, done, xsum, xchg[2 slots][4 quarters]
+  static constexpr int kNumBars = 3 + 8 + 2 + 7 + 1 + 8;
   static constexpr int kMisc = kBars + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16 + 4 * 4;
   static_assert(kOpV >= D * D * 2, "U^T is staged in a vbar^T slot");
@@ -94,7 +94,7 @@ struct CoarseSmem {
 
 struct CoarseBars {
   uint64_t *pro_full, *pro_mma, *qsq_ready, *kw_full, *kw_empty, *v_full, *v_empty, *s1full, *s2full, *s2free,
-      *pfull, *ofull, *c_full, *xfull, *done, *xchg, *xsum, *tpart;
+      *pfull, *ofull, *c_full, *xfull, *done, *xchg, *xsum;
 };
 
 __device__ __forceinline__ CoarseBars carve(uint8_t* base) {
@@ -116,8 +116,7 @@ __device__ __forceinline__ CoarseBars carve(uint8_t* base) {
   r.xfull = b + 18;
   r.done = b + 19;
   r.xsum = b + 20;
-  r.tpart = b + 21;
-  r.xchg = b + 22;  // [slot * 4 + lane quarter]
+  r.xchg = b + 21;  // [slot * 4 + lane quarter]
   return r;
 }
 
@@ -171,7 +170,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bars.pfull, 8);
     for (int i = 0; i < 8; ++i) mbar_init(bars.xchg + i, 2);  // the two warps of a lane quarter
     mbar_init(bars.xsum, 8);
-    mbar_init(bars.tpart, 4);
     mbar_init(bars.ofull, 1);
     mbar_init(bars.c_full, 1);
     mbar_init(bars.xfull, 1);
@@ -236,7 +234,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t t_s1 = tmem;          // two S1 buffers (P aliases their first 64 columns)
   const uint32_t t_s2 = tmem + 256;    // S2; the drift at the end
   const uint32_t t_o = tmem + 384;     // O; Q U in the prologue
-  constexpr uint32_t kTileQ = L::kTileQ;
 
   if (warp == 0) {
     // ================================================================ Q, U^T, (kbar, w), C_vk
