@@ -184,7 +184,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool dense_a = args.all_blocks || it.qa >= args.dense_start;
   const bool dense_b = args.all_blocks || (has_b && it.qb >= args.dense_start);
 
-  // ---- setup: barriers and TMEM
+  // ---- the two partition rows of the key-block lists: every byte load of this thread
+  // goes out first, so that their latency overlaps the barrier setup and the TMEM
+  // allocation; they are staged in shared memory below.
+  const size_t part_bank = static_cast<size_t>(it.bank) * args.nB;
+  constexpr int kPer = (kMaxKeyBlocks + kThreads - 1) / kThreads;
+  uint8_t row_va[kPer], row_vb[kPer];
+  {
+    const uint8_t* pa = dense_a ? nullptr : args.partition + (part_bank + it.qa) * args.nB;
+    const uint8_t* pb = (has_b && !dense_b) ? args.partition + (part_bank + it.qb) * args.nB : nullptr;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int j = threadIdx.x + i * kThreads;
+      row_va[i] = (pa != nullptr && j < args.dense_start) ? pa[j] : 0;
+      row_vb[i] = (pb != nullptr && j < args.dense_start) ? pb[j] : 0;
+    }
+  }
+
+  // ---- setup: barriers and TMEM; the Q tiles depend on nothing else, so their loads go
+  // out as soon as their barrier exists
   if (threadIdx.x == 0) {
     mbar_init(bars.qfull, 1);
     for (int s = 0; s < NST; ++s) {
@@ -199,13 +217,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bars.done, 1);
     *abort_flag = 0;
     fence_barrier_init();
-  }
-  if (warp == 1) tmem_alloc(tmem_slot, 512);
-  __syncthreads();
-  tc_fence_after();
-
-  // ---- the Q tiles do not depend on the key lists: load them first
-  if (threadIdx.x == 0) {
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_vt);
@@ -221,32 +232,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d_hint(sQ + kTileBytes + a * 128 * 128, &tm_q, bars.qfull, a * 64, qrow_b, stream);
     }
   }
-
-  // ---- key-block lists: stage the two partition rows (independent loads), then
-  // one warp splits them into blocks kept by both / by A only / by B only.
-  const size_t part_bank = static_cast<size_t>(it.bank) * args.nB;
-  {
-    // all of this thread's byte loads first (one latency), then the stores
-    constexpr int kPer = (kMaxKeyBlocks + kThreads - 1) / kThreads;
-    const uint8_t* pa = dense_a ? nullptr : args.partition + (part_bank + it.qa) * args.nB;
-    const uint8_t* pb = (has_b && !dense_b) ? args.partition + (part_bank + it.qb) * args.nB : nullptr;
-    uint8_t va[kPer], vb[kPer];
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int j = threadIdx.x + i * kThreads;
-      va[i] = (pa != nullptr && j < args.dense_start) ? pa[j] : 0;
-      vb[i] = (pb != nullptr && j < args.dense_start) ? pb[j] : 0;
-    }
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int j = threadIdx.x + i * kThreads;
-      if (j < args.dense_start) {
-        row_a[j] = va[i];
-        row_b[j] = vb[i];
-      }
+  for (int i = 0; i < kPer; ++i) {
+    const int j = threadIdx.x + i * kThreads;
+    if (j < args.dense_start) {
+      row_a[j] = row_va[i];
+      row_b[j] = row_vb[i];
     }
   }
-  __syncthreads();
+  __syncthreads();  // barriers, TMEM address and staged rows are visible to all
+  tc_fence_after();
   {
     // Key-block lists by a block-wide compaction in one pass: thread q takes blocks
     // 8q .. 8q + 7 (two 32-bit words of each staged row), counts its blocks kept by both
