@@ -146,9 +146,9 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
     }
   }
 
-  // Native rows of this thread's PASSES rows, then each tensor's PASSES row chunks in
-  // one burst of independent loads (two tensors in flight): the pass is bound by the
-  // latency of these gathers.
+  // Native rows of this thread's PASSES rows; each tensor's PASSES row chunks then go
+  // out in one burst of independent loads (Q to registers, K and V by asynchronous copies
+  // below), so the pass waits on one gather latency rather than one per row.
   int nat[PASSES];
 #pragma unroll
   for (int p = 0; p < PASSES; ++p) {
