@@ -256,6 +256,24 @@ int recap_coarse_tail(const void* q_reordered, const void* basis_t_bf16, const v
   return launch_center(c, s);
 }
 
+// Streaming multiprocessors of the current device (cached per device ordinal).
+static int device_sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 1;
+  if (dev >= 64) {
+    int n = 1;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 1;
+  }
+  if (counts[dev] == 0) {
+    int n = 1;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 1;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
 static int fmha_common(const void* q_reordered, const void* k_reordered, const void* v_transposed, int banks,
                        int S, int D, FmhaLaunch* L) {
   Geom g;
@@ -263,6 +281,7 @@ static int fmha_common(const void* q_reordered, const void* k_reordered, const v
   int rc = kOk;
   const int S_pad = ((S + 127) / 128) * 128;
   L->args.q = static_cast<const __nv_bfloat16*>(q_reordered);
+  L->args.num_sms = device_sm_count();
   rc |= make_tmap_bf16(&L->tm_q, q_reordered, static_cast<uint64_t>(banks) * S_pad, D, 128);
   rc |= make_tmap_bf16(&L->tm_k, k_reordered, static_cast<uint64_t>(banks) * S_pad, D, 128);
   rc |= make_tmap_bf16(&L->tm_vt, v_transposed, static_cast<uint64_t>(banks) * D, S_pad, D);

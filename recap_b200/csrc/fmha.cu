@@ -40,7 +40,6 @@ namespace {
 
 constexpr int kThreads = 320;
 constexpr int kSoftmaxWarp0 = 2;
-constexpr int kNumSmsGuess = 148;  // B200: one CTA per SM
 constexpr int kMaxKeyBlocks = 2048;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by 2^8
 // Largest logit excess over the running max (log2 units) the bounded path accepts: every
@@ -380,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // its Q tiles and partition rows into L2 now, so that its prologue does not wait on
       // HBM (a hint: a wrong guess costs 64 KB of reads).
       if (args.q != nullptr && !*abort_flag) {
-        const int nxt = blockIdx.x + kNumSmsGuess;
+        const int nxt = blockIdx.x + args.num_sms;  // one CTA per SM
         if (nxt < static_cast<int>(gridDim.x)) {
           const Item in = decode_item(args, nxt);
 #pragma unroll

@@ -156,6 +156,7 @@ struct FmhaArgs {
   const float* center;     // [banks]
   int tma_epilogue;        // 1: tm_go / tm_det describe go / det (epilogue 1 with video rows)
   const __nv_bfloat16* q;  // [banks, S_pad, D] reordered Q (the tiles tm_q reads; L2 prefetch)
+  int num_sms;             // SMs of the device: the CTA that follows this one on its SM
   int* status;
 };
 struct FmhaLaunch {
