@@ -550,39 +550,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t gate[2];
       uint32_t one;  // 1, opaque to the compiler: the mask bits below stay multiply-adds
       asm volatile("mov.b32 %0, 1;" : "=r"(one));
+      // Sixteen columns of S1 and S2 per step; the next step's TMEM loads go out before
+      // this step's logits, so their latency overlaps the arithmetic.
+      float sa1[16], sa2[16], sb1[16], sb2[16];
+      tmem_ld16(t_s1 + b * kTileN + h * kHalf + lane_base, sa1);
+      tmem_ld16(t_s2 + h * kHalf + lane_base, sa2);
+      tmem_wait_ld();
+      uint32_t gm = 0;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float v1[32], v2[32];
-        tmem_ld32(t_s1 + b * kTileN + h * kHalf + c * 32 + lane_base, v1);
-        tmem_ld32(t_s2 + h * kHalf + c * 32 + lane_base, v2);
-        tmem_wait_ld();
-        const float4* ct4 = reinterpret_cast<const float4*>(colterm + j * kTileN + h * kHalf + c * 32);
-        uint32_t gm = 0;
+      for (int k = 0; k < kHalf / 16; ++k) {
+        float (&v1)[16] = (k & 1) ? sb1 : sa1;
+        float (&v2)[16] = (k & 1) ? sb2 : sa2;
+        if (k + 1 < kHalf / 16) {
+          float (&n1)[16] = (k & 1) ? sa1 : sb1;
+          float (&n2)[16] = (k & 1) ? sa2 : sb2;
+          tmem_ld16(t_s1 + b * kTileN + h * kHalf + (k + 1) * 16 + lane_base, n1);
+          tmem_ld16(t_s2 + h * kHalf + (k + 1) * 16 + lane_base, n2);
+        }
+        const float4* ct4 = reinterpret_cast<const float4*>(colterm + j * kTileN + h * kHalf + k * 16);
 #pragma unroll
-        for (int e4 = 0; e4 < 8; ++e4) {
+        for (int e4 = 0; e4 < 4; ++e4) {
           const float4 ct = ct4[e4];
           const float cts[4] = {ct.x, ct.y, ct.z, ct.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int e = 4 * e4 + i;
-            const float quad = v2[e];
+            const int el = 4 * e4 + i;         // element of this step
+            const int e = (k & 1) * 16 + el;   // bit of the 32-column chunk's mask
+            const float quad = v2[el];
             // The gate as a branch around the gated product and the mask bit, the bit
             // set by a multiply-add with an opaque 1 (kept on the FMA pipe): this loop
             // is bound by the integer pipe, where selects of the factor and of the bit
             // cost more (bench tail 3.445 ms with selects, 3.223 with the branch and an
             // OR, 3.152 with the multiply-add).
-            const float base = fmaf(v1[e], s_l2, cts[i]);
+            const float base = fmaf(v1[el], s_l2, cts[i]);
             float xg = base;
             if (quad <= gate_max) {
               xg = fmaf(quad, h_l2, base);
               asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(gm) : "r"(one), "r"(1u << e));
             }
-            x[c * 32 + e] = xg;
+            x[k * 16 + el] = xg;
           }
         }
-        // opaque copy: the exponential phase then tests these packed bits instead of the
-        // compiler keeping 32 comparison results per word alive (which spills)
-        asm volatile("mov.b32 %0, %1;" : "=r"(gate[c]) : "r"(gm));
+        if (k & 1) {
+          // opaque copy: the exponential phase then tests these packed bits instead of the
+          // compiler keeping 32 comparison results per word alive (which spills)
+          asm volatile("mov.b32 %0, %1;" : "=r"(gate[k >> 1]) : "r"(gm));
+          gm = 0;
+        }
+        tmem_wait_ld();  // the next step's columns have landed
       }
       // S2 has been read: the next tile's quadratic term may overwrite it
       tc_fence_before();
