@@ -717,15 +717,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       // completed): row t at 2 D bytes, its 16-byte chunks XOR-swizzled by t mod 8; each
       // warp then stores its 32 half-rows as whole D-byte runs, 256 / D rows per instruction
       const uint32_t stage = smem_u32(sV);
-#pragma unroll 1
-      for (int c = 0; c < kDh / 32; ++c) {
-        float ov[32], xv[32];
-        tmem_ld32(t_o + h * kDh + c * 32 + lane_base, ov);
-        tmem_ld32(t_s2 + h * kDh + c * 32 + lane_base, xv);
-        tmem_wait_ld();
-        uint32_t w[16];
+      // 16 columns of O and of the drift per step; the next step's TMEM loads go out
+      // before this step's arithmetic.
+      float oa[16], xa[16], ob[16], xb[16];
+      tmem_ld16(t_o + h * kDh + lane_base, oa);
+      tmem_ld16(t_s2 + h * kDh + lane_base, xa);
+      tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
+      for (int k = 0; k < kDh / 16; ++k) {
+        float (&ov)[16] = (k & 1) ? ob : oa;
+        float (&xv)[16] = (k & 1) ? xb : xa;
+        if (k + 1 < kDh / 16) {
+          tmem_ld16(t_o + h * kDh + (k + 1) * 16 + lane_base, (k & 1) ? oa : ob);
+          tmem_ld16(t_s2 + h * kDh + (k + 1) * 16 + lane_base, (k & 1) ? xa : xb);
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
           float o0 = ov[2 * e] * inv_l, o1 = ov[2 * e + 1] * inv_l;
           bf16_round2(o0, o1);
           if (!has_tail) o0 = o1 = 0.f;
@@ -738,10 +746,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           w[e] = pack_bf16(o0 + g0, o1 + g1);
         }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int j = (h * kDh + c * 32) / 8 + q;  // 16-byte chunk of the row
+        for (int q = 0; q < 2; ++q) {
+          const int j = (h * kDh + k * 16) / 8 + q;  // 16-byte chunk of the row
           st_shared_v4(stage + t * (2 * D) + ((j ^ (t & 7)) << 4), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         }
+        tmem_wait_ld();  // the next step's columns have landed
       }
       __syncwarp();
       {
