@@ -98,10 +98,16 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    NVML_REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+                    0x4: "sw_power_cap"}
+
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.skip = 0
+        self.nvml = None      # NVML handle of this process's GPU, for polling while it drains
+        self.polled = []      # (sm_mhz, max_mhz, reason bits) taken by poll_until()
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"recap_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
@@ -122,6 +128,35 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _nvml_handle(self):
+        if self.nvml is None:
+            try:
+                import pynvml
+                pynvml.nvmlInit()
+                prop = torch.cuda.get_device_properties(torch.cuda.current_device())
+                bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+                self.nvml = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                self.nvml = False
+        return self.nvml or None
+
+    def poll_until(self, event: "torch.cuda.Event") -> None:
+        """Sample SM clock and clock-event reasons through NVML every few ms until `event`
+        completes: a timed region shorter than nvidia-smi's sampling period (a few short
+        steps on many GPUs) still gets samples taken while its kernels run."""
+        h = self._nvml_handle()
+        while not event.query():
+            if h is not None:
+                try:
+                    import pynvml
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.polled.append((float(sm), float(mx), int(bits)))
+                except Exception:
+                    h = None
+            time.sleep(0.002)
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -134,7 +169,9 @@ class ClockSampler:
         try:
             rows = [r.split(",") for r in self.path.read_text().strip().splitlines()[self.skip:]]
         except Exception:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+            rows = []
+            if not self.polled:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
         sm = sorted(float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit())
         mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -145,6 +182,13 @@ class ClockSampler:
             for name, val in zip(names, r[5:9]):
                 if val.strip().lower() == "active":
                     reasons.add(name)
+        for smv, mxv, bits in self.polled:
+            sm.append(smv)
+            mx.append(mxv)
+            for bit, name in self.NVML_REASONS.items():
+                if bits & bit:
+                    reasons.add(name)
+        sm.sort()
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
@@ -348,6 +392,7 @@ def run_ours(args) -> None:
         for i in range(args.steps):
             out = op.attend(0, *inputs[i % 2])
         end.record()
+        clk.poll_until(end)  # the host queued every step: sample while the GPU runs them
         torch.cuda.synchronize()
     if group is not None:
         dist.barrier(group=group)
