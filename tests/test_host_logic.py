@@ -96,3 +96,44 @@ def test_library_rejects_bad_shapes_without_a_gpu():
     # D must be 64 or 128: rejected on the host before any device call
     assert lib.recap_pool_select(None, None, 1, 4, 96, 1, 1.0, 512, 128, None, None) == _lib.RECAP_ERR_SHAPE
     assert lib.recap_closure_workspace_floats(2, 64, 2048) == 2 * 2 * 1 * 64 * 64
+
+
+def test_bench_clock_summary_merges_nvml_polls_and_reasons(tmp_path):
+    """The bench's clock record: nvidia-smi rows after the start mark plus NVML polls,
+    median SM clock, the largest max clock, and the throttle reasons either source saw."""
+    import sys
+
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    c = bench.ClockSampler(0)
+    c.path = tmp_path / "clocks.csv"
+    c.path.write_text("0, 1965, 1965, 300, 0x0, Not Active, Not Active, Not Active, Not Active\n"
+                      "0, 1800, 1965, 900, 0x4, Not Active, Not Active, Not Active, Active\n")
+    c.skip = 1  # the first row was taken before the timed region
+    c.polled = [(1700.0, 1965.0, 0x4), (1900.0, 1965.0, 0x0), (1850.0, 1965.0, 0x20)]
+    s = c.summary()
+    assert s["samples"] == 4
+    assert s["sm_mhz"] == 1850.0  # sorted 1700, 1800, 1850, 1900 -> element 2
+    assert s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap", "sw_thermal_slowdown"]
+    c.path = tmp_path / "missing.csv"
+    c.polled = []
+    assert c.summary()["samples"] == 0
+
+
+def test_bench_kept_tile_flops_counts_real_tokens():
+    """4 m n d per kept 128x128 tile, with the partial last block's real token count and the
+    shared text row and column always counted."""
+    import sys
+
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    nv, S, d = 300, 310, 64  # blocks of 128, 128, 44 video tokens + 10 text: NB = 3, shared last block
+    part = torch.zeros(1, 1, 3, 3, dtype=torch.bool)
+    part[0, 0, 0, 1] = True
+    counts = [128.0, 128.0, 54.0]
+    want = 4 * d * (counts[0] * counts[1] + sum(counts[i] * counts[2] for i in range(2)) +
+                    sum(counts[2] * counts[j] for j in range(3)))
+    assert bench.kept_tile_flops(part, S, nv, d) == pytest.approx(want)
