@@ -42,6 +42,7 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true", help="skip the CPU oracle check of the last timed output")
     p.add_argument("--profile-steps", type=int, default=3, help="extra steps with per-kernel CUDA events")
     p.add_argument("--heads", type=int, default=None,
                    help="run only this many of the layer's heads (small cases for ncu captures)")
@@ -102,8 +103,13 @@ class ClockSampler:
     NVML_REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
                     0x4: "sw_power_cap"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, bus_id: str | None = None):
+        # nvidia-smi's --id reads a bare index as a physical GPU index, which is not this
+        # process's GPU under CUDA_VISIBLE_DEVICES: name the device by its PCI bus id
+        if bus_id is None:
+            prop = torch.cuda.get_device_properties(torch.cuda.current_device())
+            bus_id = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+        self.bus_id = bus_id
         self.proc = None
         self.skip = 0
         self.nvml = None      # NVML handle of this process's GPU, for polling while it drains
@@ -113,7 +119,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--id={self.bus_id}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
             # nvidia-smi takes a while to start: begin the timed region once it samples,
             # and count only the samples taken from then on
@@ -133,9 +139,7 @@ class ClockSampler:
             try:
                 import pynvml
                 pynvml.nvmlInit()
-                prop = torch.cuda.get_device_properties(torch.cuda.current_device())
-                bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
-                self.nvml = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+                self.nvml = pynvml.nvmlDeviceGetHandleByPciBusId(self.bus_id.encode())
             except Exception:
                 self.nvml = False
         return self.nvml or None
@@ -318,6 +322,47 @@ def end_to_end(op, host, steps: int, group, world: int, n_heads: int, S: int, d:
             "serial_value": round(t_serial, 1)}
 
 
+def workload_config(w: dict, world: int) -> dict:
+    """The ``config`` of both arms' JSON lines."""
+    nv = w["grid"][0] * w["grid"][1] * w["grid"][2]
+    nb = (nv + 127) // 128
+    return {"workload": w["name"], "heads": w["heads"], "head_dim": w["dim"], "video_tokens": nv,
+            "text_tokens": w["text"], "seq_len": nv + w["text"], "key_blocks": nb,
+            "keep": max(1, round(w["density"] * nb)), "parallelism": f"heads/{world}", "bank": "HBM",
+            "l2": "inputs 2.19 GB per step > 126 MB L2 (no flush needed)"}
+
+
+def parity_leg(w: dict, layout, hx: dict, basis, part0, part2, keep: bool, out_rows: dict, oracle_qblocks) -> dict:
+    """The last timed SPARSE output of the sampled banks against the block oracle on the
+    CPU (oracle/block_oracle.py), replaying the REFRESH on x0, the revalidating REFRESH on
+    x2 and the SPARSE step on the last timed inputs."""
+    from oracle import block_oracle as bo
+
+    t0 = time.perf_counter()
+    perm = layout.permutation
+    orc_ = bo.BlockOracle(perm, w["text"], w["text_first"], w["density"], qblocks=oracle_qblocks)
+    fwd = orc_.fwd
+    nv = layout.video_tokens
+    mism = bo.selection_mismatches(part0, hx["x0"][0][:, fwd], hx["x0"][1][:, fwd], w["density"], nv)
+    orc_.refresh(*hx["x0"], basis=basis, partition=part0)
+    orc_.step = 1
+    if not keep:
+        mism += bo.selection_mismatches(part2, hx["x2"][0][:, fwd], hx["x2"][1][:, fwd], w["density"], nv)
+    orc_.refresh(*hx["x2"], decision=keep, new_partition=None if keep else part2)
+    orc_.step = 2
+    exp = orc_.sparse(*hx["last"])
+    got = torch.cat([out_rows[qb].reshape(-1) for qb in sorted(exp)])
+    ref = torch.cat([exp[qb].reshape(-1) for qb in sorted(exp)])
+    c = bo.compare_bf16(got, ref)
+    return {"max_abs": round(c["max_abs"], 5), "mean_rel": round(c["mean_rel"], 6),
+            "elements": c["n"], "elements_over_2e-2": c["n_over_2e-2"],
+            "max_bf16_ulps_over_2e-2": round(c["max_ulps_over_2e-2"], 3), "max_abs_ref": round(c["max_abs_ref"], 3),
+            "selection_mismatches_beyond_ties": mism, "banks": hx["banks"], "query_blocks": len(exp),
+            "cpu_s": round(time.perf_counter() - t0, 1),
+            "checked": "last timed SPARSE output, sampled banks x query blocks (every dense block), "
+                       "against the CPU block oracle replaying REFRESH(x0) -> REFRESH(x2) -> SPARSE"}
+
+
 # ----------------------------------------------------------------------------- our arm
 
 
@@ -363,19 +408,42 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     x1 = perturbed(x0, 1, dev)
     x2 = perturbed(x1, 2, dev)
+    check = rank == 0 and not args.no_parity
+    hx: dict = {}
+    if check:
+        # two banks of rank 0 (its first and last head) for the parity leg, on the host
+        sb = sorted({0, len(hs) - 1})
+        hx = {"banks": sb, **{n: [t[0, sb].float().cpu() for t in x] for n, x in (("x0", x0), ("x1", x1), ("x2", x2))}}
+        hx["part0"] = op.banks[0][0].partition[0, sb].cpu().clone()
+        hx["basis"] = op.layers[0][0].basis[sb].cpu().clone()
+    part0_dev = op.banks[0][0].partition.clone()
     del x0
     inputs = [x1, x2]
 
-    # refresh timing (revalidating refresh on x2, then restore the bank state with x1's)
+    # refresh timing: a revalidating refresh on x2, device time from a common start (the
+    # ranks meet at a barrier first), max over ranks; per-call times beside it
     op.begin_step(1, REFRESH)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if group is not None:
+        dist.barrier(group=group)
+    op.launches.timing = True
     t0.record()
     op.attend(0, *x2)
     t1.record()
     torch.cuda.synchronize()
-    refresh_ms = t0.elapsed_time(t1)
+    op.launches.timing = False
+    refresh_times = op.launches.take_times()
+    refresh_t = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
+    if group is not None:
+        dist.all_reduce(refresh_t, op=dist.ReduceOp.MAX, group=group)
+    refresh_ms = float(refresh_t.item())
     op.drain_validation()
+    keep = bool(torch.equal(op.banks[0][0].partition, part0_dev))
+    if check:
+        hx["part2"] = op.banks[0][0].partition[0, hx["banks"]].cpu().clone()
+    del part0_dev
 
     op.begin_step(2, SPARSE)
     for i in range(args.warmup):
@@ -386,7 +454,7 @@ def run_ours(args) -> None:
     launches_before = op.launches.count
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clk:
+    with ClockSampler() as clk:
         torch.cuda.synchronize()
         start.record()
         for i in range(args.steps):
@@ -401,6 +469,15 @@ def run_ours(args) -> None:
     if group is not None:
         dist.all_reduce(elapsed, op=dist.ReduceOp.MAX, group=group)
     ms_per_step = float(elapsed.item()) / args.steps
+    out_rows = None
+    if check:
+        from oracle.block_oracle import BlockOracle, sample_qblocks
+
+        oracle_qblocks = sample_qblocks(nv, S, 8)
+        fwd = BlockOracle(layout.permutation, w["text"], w["text_first"], w["density"], qblocks=[]).fwd
+        sel = out[0, hx["banks"]]
+        out_rows = {qb: sel[:, fwd[qb * 128: min(S, (qb + 1) * 128)].to(dev)].float().cpu() for qb in oracle_qblocks}
+        hx["last"] = hx["x1"] if (args.steps - 1) % 2 == 0 else hx["x2"]
     del out
 
     # per-kernel times over a few more steps (events on the launching stream)
@@ -429,6 +506,11 @@ def run_ours(args) -> None:
         del host
     op.check_device_status()
 
+    parity = None
+    if check:
+        parity = parity_leg(w, layout, hx, hx["basis"], hx["part0"], hx["part2"], keep, out_rows, oracle_qblocks)
+    del hx, out_rows
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle.cpu_baseline import time_sparse_sample
@@ -442,12 +524,11 @@ def run_ours(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded smooth low-rank (rank 16) + 0.5 noise Q/K/V, 0.05 perturbation per step",
-            "config": {"workload": w["name"], "heads": H, "head_dim": d, "video_tokens": nv, "text_tokens": w["text"],
-                       "seq_len": S, "key_blocks": geo.n_blocks, "keep": max(1, round(w["density"] * geo.n_blocks)),
-                       "parallelism": f"heads/{world}", "bank": "HBM",
-                       "l2": "inputs 2.19 GB per step > 126 MB L2 (no flush needed)"},
+            "config": workload_config(w, world),
             "dense_equiv_tflops": round(dense_flops / (ms_per_step * 1e-3) / 1e12, 1),
             "refresh_us": round(refresh_ms * 1000.0, 1),
+            "refresh_kernels_ms": {k: round(sum(v), 4) for k, v in refresh_times.items()},
+            "refresh_rerank": not keep,
             "kernels_ms": {k: round(v, 4) for k, v in kernels_ms.items()},
             "roofline": {
                 "kernel": "recap_sparse_step (block-sparse FMHA + corrected merge)",
@@ -461,6 +542,7 @@ def run_ours(args) -> None:
             "gpu_launches": gpu_launches,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "parity": parity,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -479,7 +561,8 @@ def run_reference(args) -> None:
         return
     from oracle.cpu_baseline import reference_arm
 
-    line = reference_arm(WORKLOAD, METRIC, UNIT, steps=args.steps, warmup=args.warmup)
+    line = reference_arm(WORKLOAD, METRIC, UNIT, steps=args.steps, warmup=args.warmup,
+                         config=workload_config(WORKLOAD, world))
     line.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup})
     print(json.dumps(line), flush=True)
 

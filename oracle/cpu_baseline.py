@@ -1,17 +1,22 @@
-"""Timed CPU baseline of the corrected SPARSE step - test/benchmark infrastructure only.
+"""Timed CPU baselines of the corrected SPARSE step - test/benchmark infrastructure only.
 
 The reference has no CPU implementation of its operator (its head is a CUDA extension
 and its other kernels are Triton), so the CPU path timed here is the oracle restatement
 of the reference's algorithm (``oracle/recap_oracle.py``), in fp32 torch on all host
-threads.  A full HunyuanVideo-720p layer call is minutes of CPU work, so one step times a
-bounded sample and scales it to one layer call:
+threads.  Two forms:
 
-* per bank, the work over the whole sequence (layout gather, block pooling of K and V,
-  per-block key variances in the basis, C_vk) is timed on ``heads`` banks;
-* per query block, the work over its rows (qsq/drift rows, coarse tail, block-sparse head
-  over its kept key blocks, merge) is timed on ``video_qblocks`` evenly spaced video query
-  blocks and ``dense_qblocks`` of the dense (text / shared-boundary) query blocks;
-* the layer-call estimate is  H * (t_bank + n_video_qb * t_video_qb + n_dense_qb * t_dense_qb).
+* ``FullLayer``: one whole SPARSE layer call, every bank and every query block, no
+  sampling (about a minute or more at HunyuanVideo-720p); ``bench.py --impl reference``
+  times it.
+* ``SampledLayer``: a bounded sample scaled to one layer call, for the GPU arm's
+  ``cpu_baseline`` (10-30 s of CPU work) and as a check of its own cost model against the
+  whole call:
+  - per bank, the work over the whole sequence (layout gather, block pooling of K and V,
+    per-block key variances in the basis, C_vk) is timed on ``heads`` banks;
+  - per query block, the work over its rows (qsq/drift rows, coarse tail, block-sparse head
+    over its kept key blocks, merge) is timed on ``video_qblocks`` evenly spaced video query
+    blocks and ``dense_qblocks`` of the dense (text / shared-boundary) query blocks;
+  - the layer-call estimate is  H * (t_bank + n_video_qb * t_video_qb + n_dense_qb * t_dense_qb).
 """
 
 from __future__ import annotations
@@ -202,6 +207,152 @@ def _cross_f32(k_r, v_r, km, counts, nv):
     return torch.bmm(v_r[:, :nv].transpose(1, 2), c) / counts.sum()
 
 
+class FullLayer:
+    """The oracle port's whole SPARSE layer call - every bank, every query block, no
+    sampling - in fp32 torch on all host threads: the timed step of ``bench.py --impl
+    reference``.
+
+    ``setup()`` (untimed) builds, per bank, the state a SPARSE step reads from the REFRESH
+    before it (recap/operator.py:331-473): the partition, the ordered covariance basis and
+    the coarse log-mass of every cached row on the refresh inputs.  The refinement of the
+    cached rows is left at zero: its values do not change the arithmetic of the step, and
+    computing it needs the dense pass over every row (174 TFLOP at config 4, far beyond a
+    bounded CPU run).  ``step()`` then runs recap/operator.py:478-527 for every bank: the
+    reorder, block pooling, per-block variances in the basis and C_vk, qsq and drift, the
+    coarse tail of every cached row, the block-sparse head of every query block over its
+    kept key blocks, the drift-weighted merge and the restore."""
+
+    def __init__(self, spec: dict, seed: int = 0, heads: int | None = None):
+        from recap_b200.sparse.geometry import hilbert_permutation  # host-side numpy only
+
+        self.spec = spec
+        self.perm = hilbert_permutation(spec["grid"])
+        self.nv = len(self.perm)
+        self.text = spec["text"]
+        self.text_first = spec["text_first"]
+        self.S = self.nv + self.text
+        self.d = spec["dim"]
+        self.scale = 1.0 / math.sqrt(self.d)
+        self.nB = (self.nv + BLOCK - 1) // BLOCK
+        self.NB = (self.S + BLOCK - 1) // BLOCK
+        self.rows = (self.nv // BLOCK) * BLOCK
+        self.heads = spec["heads"] if heads is None else int(heads)
+        self.seed = seed
+        self.fwd, self.inv = orc.gather_indices(torch.as_tensor(self.perm), self.text, self.text_first)
+        torch.set_num_threads(host_threads())
+        self.state: list[dict] = []
+        self.inputs: list[tuple] = []
+
+    def _bank_inputs(self, h: int):
+        x0 = [t[0, 0] for t in orc.smooth_lowrank(self.spec["grid"], self.spec["heads"], self.d, self.text,
+                                                   self.text_first, self.seed, head_slice=slice(h, h + 1))]
+        x1 = [orc.perturb_heads(t[None, None], seed=1, tensor=i, head_offset=h)[0, 0] for i, t in enumerate(x0)]
+        return x0, x1
+
+    def setup(self) -> None:
+        """Untimed: per bank, the REFRESH state on the first inputs, and the step's inputs."""
+        self.state, self.inputs = [], []
+        for h in range(self.heads):
+            x0, x1 = self._bank_inputs(h)
+            q_r, k_r, v_r = (t.float()[self.fwd] for t in x0)
+            part = orc.head_partition(q_r[None], k_r[None], self.scale, self.spec["density"], self.nv)[0]
+            km, counts = orc.pool_blocks(k_r[None], self.nv)
+            b0 = orc.closure_basis(orc.within_block_scatter(k_r[None], km, counts, self.nv))
+            basis, _ = orc.order_basis(b0, _rotated_variance_f32(k_r[None], b0, self.nv), counts)
+            st = dict(partition=part, basis=basis[0])
+            _, gl, _ = self._coarse(q_r, k_r, v_r, st)
+            st.update(ogl=gl, det=torch.zeros(self.rows, self.d, dtype=torch.float16), dl=torch.zeros(self.rows))
+            self.state.append(st)
+            self.inputs.append(tuple(x1))  # model dtype (bf16), native order
+
+    def _coarse(self, q_r, k_r, v_r, st):
+        """Closure statistics and the coarse tail of every cached row (fp32, the
+        reference's bf16 rounding points)."""
+        nv, rows, d, sc = self.nv, self.rows, self.d, self.scale
+        bf = torch.bfloat16
+
+        def rd(x):
+            return x.to(bf).float()
+
+        km, counts = orc.pool_blocks(k_r[None], nv)
+        vm, _ = orc.pool_blocks(v_r[None], nv)
+        var = orc.fold_rank(_rotated_variance_f32(k_r[None], st["basis"][None], nv), 4)[0]
+        cvk = _cross_f32(k_r[None], v_r[None], km, counts, nv)[0]
+        qv = rd(q_r[:rows])
+        qsq = rd(rd(qv @ rd(st["basis"])) ** 2)
+        drift = rd(sc * rd(qv @ rd(cvk).T))
+        kb, vb, wb = rd(km[0]), rd(vm[0]), rd(var)
+        logn = torch.log(counts.float())
+        go = torch.empty(rows, d)
+        gl = torch.empty(rows)
+        s2 = sc * sc
+        nqb = rows // BLOCK
+        for c0 in range(0, nqb, 32):
+            c1 = min(nqb, c0 + 32)
+            r0, r1 = c0 * BLOCK, c1 * BLOCK
+            s = (qv[r0:r1] @ kb.T) * sc + logn
+            quad = qsq[r0:r1] @ wb.T
+            gate = quad * s2 <= 4.0
+            s = s + torch.where(gate, quad * (0.5 * s2), torch.zeros_like(quad))
+            s.masked_fill_(st["partition"][c0:c1].repeat_interleave(BLOCK, dim=0), -math.inf)
+            m = s.max(-1, keepdim=True).values
+            m = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+            p = torch.exp(s - m)
+            l = p.sum(-1, keepdim=True)
+            g = (p * gate).sum(-1, keepdim=True) / l
+            o = rd((rd(p) @ vb) / l)
+            go[r0:r1] = rd(o + rd(rd(g) * drift[r0:r1]))
+            gl[r0:r1] = (m + torch.log(l)).squeeze(-1)
+        return go, gl, counts
+
+    def sparse_bank(self, q, k, v, st: dict) -> torch.Tensor:
+        """One bank's SPARSE call: native [S, d] model-dtype inputs in, native fp32 out."""
+        q_r, k_r, v_r = (t.float()[self.fwd] for t in (q, k, v))
+        S, d, sc, rows = self.S, self.d, self.scale, self.rows
+        go, gl, _ = self._coarse(q_r, k_r, v_r, st)
+        center = (gl - st["ogl"]).mean()
+        kmask = orc.kernel_block_mask(st["partition"][None], S, self.nv)[0]
+        pad = self.NB * BLOCK - S
+        kp = torch.nn.functional.pad(k_r, (0, 0, 0, pad)).view(self.NB, BLOCK, d)
+        vp = torch.nn.functional.pad(v_r, (0, 0, 0, pad)).view(self.NB, BLOCK, d)
+        oh = torch.empty(S, d)
+        lh = torch.empty(S)
+        for i in range(self.NB):
+            r0, r1 = i * BLOCK, min(S, (i + 1) * BLOCK)
+            blocks = torch.nonzero(kmask[i]).flatten()
+            s = (q_r[r0:r1] @ kp[blocks].reshape(-1, d).T) * sc
+            if pad and bool(blocks[-1] == self.NB - 1):
+                s[:, -pad:] = -math.inf  # padding past the end of the sequence
+            m = s.max(-1, keepdim=True).values
+            p = torch.exp(s - m)
+            l = p.sum(-1, keepdim=True)
+            oh[r0:r1] = (p @ vp[blocks].reshape(-1, d)) / l
+            lh[r0:r1] = (m + torch.log(l)).squeeze(-1)
+        oh = oh.to(torch.bfloat16).float()
+        out = oh.clone()
+        if rows:
+            admit = torch.exp(-(gl - st["ogl"] - center).abs())
+            cl = gl + st["dl"]
+            tc = torch.maximum(gl, cl)
+            ms = (1 - admit) * torch.exp(gl - tc)
+            mc = admit * torch.exp(cl - tc)
+            den = torch.clamp(ms + mc, min=1e-30)
+            tail_o = (go * ms[:, None] + (go + st["det"].float()) * mc[:, None]) / den[:, None]
+            tail_l = tc + torch.log(den)
+            c = torch.maximum(lh[:rows], tail_l)
+            wh = torch.exp(lh[:rows] - c)
+            wt = torch.exp(tail_l - c)
+            out[:rows] = (oh[:rows] * wh[:, None] + tail_o * wt[:, None]) / torch.clamp(wh + wt, min=1e-30)[:, None]
+        return out.to(torch.bfloat16).float()[self.inv]
+
+    def step(self) -> float:
+        """One whole SPARSE layer call over every bank; returns its wall seconds."""
+        t0 = time.perf_counter()
+        for x, st in zip(self.inputs, self.state):
+            self.sparse_bank(*x, st)
+        return time.perf_counter() - t0
+
+
 def time_sparse_sample(op=None, inputs=None, layout=None, spec=None, repeats: int = 2) -> dict:
     """cpu_baseline entry for bench.py: median of ``repeats`` sampled steps, scaled."""
     runner = SampledLayer(spec)
@@ -212,23 +363,39 @@ def time_sparse_sample(op=None, inputs=None, layout=None, spec=None, repeats: in
             "torch_threads": torch.get_num_threads(), "kind": "port", "sample": runner.sample_text()}
 
 
-def reference_arm(spec: dict, metric: str, unit: str, steps: int, warmup: int) -> dict:
-    """``bench.py --impl reference``: the reference's CPU path (the oracle port) on all host
-    threads, one sampled SPARSE step per benchmark step, scaled to one layer call."""
+def reference_arm(spec: dict, metric: str, unit: str, steps: int, warmup: int, config: dict | None = None) -> dict:
+    """``bench.py --impl reference``: the reference's CPU path (the oracle port, fp32 torch on
+    all host threads) on the same workload as the GPU arm.
+
+    The timed region is ONE whole, unsampled SPARSE layer call (``FullLayer.step``: every
+    bank, every query block), whatever ``steps`` asks: a layer call is a minute or more of
+    CPU work, so the run reports ``steps_timed`` = 1.  The ``warmup`` steps run on the
+    bounded sample of ``SampledLayer``, whose scaled figure is reported beside the value as
+    a check of its cost model (``sampled_estimate_us``)."""
     runner = SampledLayer(spec)
     runner.refresh()
-    for _ in range(warmup):
+    for _ in range(max(1, warmup)):
         runner.step()
-    t0 = time.perf_counter()
-    vals = [runner.layer_us(runner.step(), spec["heads"]) for _ in range(steps)]
-    wall = time.perf_counter() - t0
-    value = round(float(np.mean(vals)), 1)
+    est = sorted(runner.layer_us(runner.step(), spec["heads"]) for _ in range(2))
+    sampled = est[len(est) // 2]
+    full = FullLayer(spec)
+    t_setup = time.perf_counter()
+    full.setup()
+    t_setup = time.perf_counter() - t_setup
+    wall = full.step()
+    value = round(wall * 1e6, 1)
     return {
         "impl": "reference", "metric": metric, "value": value, "unit": unit, "higher_is_better": False,
-        "ms_per_step": round(value / 1000.0, 3), "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (same generator as the GPU arm, CPU)",
-        "config": {"workload": spec["name"], "heads": spec["heads"], "head_dim": spec["dim"]},
-        "cpu_baseline": {"value": value, "unit": unit, "kind": "port", "cores": host_threads(),
-                         "sample": runner.sample_text(), "sample_wall_s_per_step": round(wall / steps, 2)},
+        "ms_per_step": round(value / 1000.0, 3), "steps_timed": 1, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (the GPU arm's generator restated on the CPU)",
+        "config": config if config is not None else {"workload": spec["name"]},
+        "cpu_baseline": {
+            "value": value, "unit": unit, "kind": "port", "cores": host_threads(),
+            "torch_threads": torch.get_num_threads(),
+            "sample": f"one whole SPARSE layer call: {full.heads} banks x all {full.NB} query blocks, no sampling "
+                      f"(refresh state built untimed in {t_setup:.0f} s)",
+            "sampled_estimate_us": round(sampled, 1),
+            "sampled_estimate_sample": runner.sample_text(),
+        },
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

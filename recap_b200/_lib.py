@@ -111,7 +111,14 @@ def check(rc: int, what: str) -> None:
             f"{what}: the problem needs more validation scratch than the library's fixed array "
             "holds (banks * ceil(rows / 32) must be <= 131072)"
         )
-    raise RuntimeError(f"{what}: CUDA launch failed (code {rc})")
+    if rc == RECAP_ERR_DEVICE:
+        raise RuntimeError(
+            f"{what}: a kernel gave up a bounded on-chip wait (device timeout); the status word "
+            "names the wait (Operator.check_device_status raises with its name)"
+        )
+    if rc == RECAP_ERR_LAUNCH:
+        raise RuntimeError(f"{what}: CUDA launch or API call failed")
+    raise RuntimeError(f"{what}: failed with status {rc}")
 
 
 def call(name: str, *args) -> None:

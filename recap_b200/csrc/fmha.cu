@@ -722,6 +722,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (in_seq && args.lse) args.lse[bank_rows + pos] = lse_h;
     }
   }
+  // Nothing asynchronous is in flight past this barrier, on the normal path and after an
+  // abort alike: the producer waited (bounded) for the completion of every TMA load it
+  // issued - at most NST can be outstanding, since each load into a slot first waited for
+  // that slot's previous load to be consumed - and the Q tiles; the MMA warp committed
+  // every MMA it issued to `done` and waited (bounded) for it; the softmax warps' TMEM
+  // loads and stores completed at their wait::ld / wait::st.  Only then is TMEM freed.
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

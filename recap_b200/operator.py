@@ -69,6 +69,14 @@ def validation_reduce(total: torch.Tensor, group=None) -> tuple[float, float]:
     return numerator, denominator
 
 
+def _bank_fits(bank: "DetailBank", sh) -> bool:
+    """Whether a bank's partition and refinement have this call's shapes."""
+    return (bank.partition is not None and tuple(bank.partition.shape) == (sh.batch, sh.heads, sh.nB, sh.nB)
+            and bank.value is not None and tuple(bank.value.shape) == (sh.banks, sh.rows, sh.D)
+            and bank.log_mass is not None and bank.coarse_lse is not None
+            and tuple(bank.coarse_lse.shape) == (sh.banks, sh.rows))
+
+
 @dataclass
 class DetailBank:
     """One layer's cached refinement and its partition (recap/operator.py:33-59)."""
@@ -308,6 +316,10 @@ class Operator:
         status = self.status_word(dev)
         inputs = layer.prepare(query, key, value, q_mean=True)
         sh = inputs.shapes
+        if bank.valid and not _bank_fits(bank, sh):
+            # A refinement of another shape cannot be scored against this call (the
+            # reference fails on the mismatch): start over as a first refresh.
+            bank.release()
         revalidating = bank.valid
         if not revalidating:
             bank.set_partition(layer.head_partition(inputs, scale), sh.S, sh.n_video)

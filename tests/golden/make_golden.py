@@ -1,7 +1,7 @@
 """Generate the golden fixtures of tests/golden/ from the REFERENCE implementation.
 
-Run in a container that has the reference tree (default /root/reference, or
-RECAP_REFERENCE_PATH):  ``python tests/golden/make_golden.py``.
+Run where a checkout of the reference tree exists, named by the environment variable
+RECAP_REFERENCE_PATH:  ``RECAP_REFERENCE_PATH=<checkout> python tests/golden/make_golden.py``.
 
 The reference operator (lyraxtg/RECAP ``recap.operator.Operator``) is driven on CPU, fp32,
 through its own Python code.  Its GPU-only steps are run as follows:
@@ -31,7 +31,9 @@ os.environ["TRITON_INTERPRET"] = "1"
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("RECAP_REFERENCE_PATH", "/root/reference"))
+if not os.environ.get("RECAP_REFERENCE_PATH"):
+    raise SystemExit("set RECAP_REFERENCE_PATH to a checkout of the reference tree (lyraxtg/RECAP)")
+REF = Path(os.environ["RECAP_REFERENCE_PATH"])
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REF))
 

@@ -106,7 +106,7 @@ def test_bench_clock_summary_merges_nvml_polls_and_reasons(tmp_path):
     sys.path.insert(0, str(REPO))
     import bench
 
-    c = bench.ClockSampler(0)
+    c = bench.ClockSampler("00000000:00:00.0")
     c.path = tmp_path / "clocks.csv"
     c.path.write_text("0, 1965, 1965, 300, 0x0, Not Active, Not Active, Not Active, Not Active\n"
                       "0, 1800, 1965, 900, 0x4, Not Active, Not Active, Not Active, Active\n")

@@ -1,6 +1,7 @@
-"""Wiring of recap_b200 into the reference package (runs where the reference tree is
-importable: RECAP_REFERENCE_PATH or /root/reference; skipped elsewhere).  No GPU: only
-construction and the host-side state machine are exercised."""
+"""Wiring of recap_b200 into the reference package.  Runs where the environment variable
+RECAP_REFERENCE_PATH names a checkout of the reference tree (lyraxtg/RECAP), and is
+skipped elsewhere.  No GPU: only construction and the host-side state machine are
+exercised."""
 
 import os
 import sys
@@ -8,8 +9,10 @@ from pathlib import Path
 
 import pytest
 
-REF = Path(os.environ.get("RECAP_REFERENCE_PATH", "/root/reference"))
-pytestmark = pytest.mark.skipif(not (REF / "recap" / "__init__.py").exists(), reason="reference tree not present")
+_REF_ENV = os.environ.get("RECAP_REFERENCE_PATH")
+REF = Path(_REF_ENV) if _REF_ENV else None
+pytestmark = pytest.mark.skipif(REF is None or not (REF / "recap" / "__init__.py").exists(),
+                                reason="RECAP_REFERENCE_PATH does not name a reference checkout")
 
 
 @pytest.fixture(scope="module")
