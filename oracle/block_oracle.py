@@ -37,6 +37,19 @@ from . import recap_oracle as orc
 
 BLOCK = 128
 
+# Coarse-tail rows that any two implementations may legitimately compute differently
+# (recap/kernels/coarse_tail.py:36-186).  The gated quadratic term s^2 qsq.w / 2 is built
+# from bf16 operands that each side rounds on its own way there: q.U and the per-block
+# variances w are fp32 sums rounded to bf16, and a value near a bf16 midpoint may round
+# either way, moving that operand by up to 2^-8 relative.  Such a flip shifts a gated
+# block's logit by up to about 0.02 nats and, for a gate within about 1% of its threshold
+# (s^2 qsq.w <= theta^2), may switch the gate (a step of up to theta^2 / 2 = 2 nats).  A row
+# whose coarse LSE differs from this oracle's by more than FLIP_LSE (about one row in ten
+# thousand) is therefore held only to a loose bound in the parity tests, as fp ties are
+# exempt in the top-k; NEAR_GATE is the margin reported as a likely gate switch.
+NEAR_GATE = 1e-2
+FLIP_LSE = 5e-4
+
 
 def _rd(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return x.to(dtype).float() if dtype != torch.float32 else x.float()
@@ -110,6 +123,9 @@ class BlockOracle:
         self.state = BankState()
         self.step = 0
         self.trace: dict = {}
+        # per (bank, cached row): the smallest relative margin |s^2 qsq.w - theta^2| / theta^2
+        # of any omitted block's gate, over the coarse evaluations of the last call
+        self.gate_margin: torch.Tensor | None = None
 
     # -- helpers --------------------------------------------------------------------------
 
@@ -137,17 +153,19 @@ class BlockOracle:
         qsq = orc.rotated_query_square(q_r[:, :self.rows], st.basis, self.dtype)  # cached rows
         dt = self.dtype
         return dict(km=km, counts=counts, cvk=cvk, qsq=qsq, kb=_rd(km, dt).double(), vb=_rd(vm, dt).double(),
-                    wb=_rd(var, dt).double(), logn=torch.log(counts.float()).double())
+                    wb=_rd(var, dt).double(), logn=torch.log(counts.float()).double(), basis=st.basis)
 
     def _coarse_bank(self, b, ctx, q_r, partition, scale, rows_sel=None, drift=None):
         """Coarse tail of bank ``b`` (recap/kernels/coarse_tail.py:36-186, 237-298, the
         gated logits of ``recap_oracle.coarse_tail``): LSE over every cached row and, for
         ``rows_sel`` (a list of query blocks), the output rows.  Returns
-        (lse [rows], {qb: out [128, d]})."""
+        (lse [rows], {qb: out [128, d]}, gate margin [rows])."""
         dt = self.dtype
         kb, wb, vb, logn = ctx["kb"][b], ctx["wb"][b], ctx["vb"][b], ctx["logn"]
         s2 = scale * scale
+        th2 = self.theta * self.theta
         lse = torch.full((self.rows,), -math.inf, dtype=torch.float32)
+        margin = torch.full((self.rows,), math.inf, dtype=torch.float64)
         outs = {}
         want = set(rows_sel or [])
         chunk = 32  # query blocks per chunk
@@ -162,6 +180,7 @@ class BlockOracle:
             gate = quad * s2 <= self.theta * self.theta
             s = s + torch.where(gate, quad * (0.5 * s2), torch.zeros_like(quad))
             omitted = (~partition[b, c0:c1]).repeat_interleave(BLOCK, dim=0)
+            margin[r0:r1] = ((quad * s2 - th2).abs() / th2).masked_fill(~omitted, math.inf).min(-1).values
             s = s.masked_fill(~omitted, -math.inf)
             m = s.max(-1, keepdim=True).values
             has = torch.isfinite(m)
@@ -182,7 +201,22 @@ class BlockOracle:
                 o = _rd(((_rd(pl.float(), dt).double() @ vb) / ll).float(), dt)
                 gd = _rd(_rd(g.float(), dt) * drift[qb].float(), dt)
                 outs[qb] = _rd(o + gd, dt)
-        return lse, outs
+        return lse, outs, margin
+
+    def _note_margin(self, margin: torch.Tensor) -> None:
+        """Gate margins of the call's coarse tail (the evaluation that defines its coarse LSE)."""
+        self.trace["gate_margin"] = margin
+        self.gate_margin = margin
+
+    def gate_flips(self, gpu_lse: torch.Tensor) -> tuple[torch.Tensor, int]:
+        """Rows of the last call whose coarse LSE (the operator's ``gpu_lse`` [banks, rows]
+        against this oracle's) differs by more than FLIP_LSE: (flags [banks, rows], how many
+        of them have a gate within NEAR_GATE of its threshold)."""
+        mine = self.trace["coarse_lse"].float()
+        theirs = gpu_lse.float()
+        same_inf = torch.isinf(theirs) & (theirs == mine)
+        flip = ((theirs - mine).abs() > FLIP_LSE) & ~same_inf
+        return flip, int((flip & (self.trace["gate_margin"] < NEAR_GATE)).sum())
 
     def _drift_rows(self, ctx, q_r, b, qb, scale):
         q = q_r[b:b + 1, qb * BLOCK:(qb + 1) * BLOCK]
@@ -220,6 +254,7 @@ class BlockOracle:
         banks, _, d = q.shape
         scale = 1.0 / math.sqrt(d)
         st = self.state
+        self.trace = {}
         q_r, k_r, v_r = self._reorder(q), self._reorder(k), self._reorder(v)
         revalidating = st.valid
         if not revalidating:
@@ -234,15 +269,17 @@ class BlockOracle:
         def write(partition, validate_with=None):
             kmask = self._kernel_mask(partition)
             lse_all = torch.empty(banks, self.rows)
+            margin = torch.empty(banks, self.rows, dtype=torch.float64)
             values, masses = {}, {}
             err = torch.zeros(2, dtype=torch.float64)
             center = None
             per_bank = []
             for b in range(banks):
                 drift = {qb: self._drift_rows(ctx, q_r, b, qb, scale) for qb in video}
-                lse_b, outs = self._coarse_bank(b, ctx, q_r, partition, scale, video, drift)
+                lse_b, outs, margin[b] = self._coarse_bank(b, ctx, q_r, partition, scale, video, drift)
                 lse_all[b] = lse_b
                 per_bank.append(outs)
+            self._note_margin(margin)
             if validate_with is not None:
                 center = orc.drift_center(lse_all, validate_with)
             for qb in video:
@@ -268,7 +305,7 @@ class BlockOracle:
 
         old_lse = st.coarse_lse if revalidating else None
         lse_all, values, masses, stats, center = write(st.partition, old_lse)
-        self.trace = dict(center=center, coarse_lse=lse_all)
+        self.trace.update(center=center, coarse_lse=lse_all)
         st.value, st.log_mass = values, masses
         if stats is not None:
             st.pending = (self.step - st.refreshed_at, stats)
@@ -280,8 +317,9 @@ class BlockOracle:
             keep = (kept / total >= self.min_overlap) if decision is None else bool(decision)
             if not keep:
                 st.partition = new if new_partition is None else new_partition.clone()
-                lse_all, values, masses, _, _ = write(new, None)
+                lse_all, values, masses, _, _ = write(st.partition, None)
                 st.value, st.log_mass = values, masses
+                self.trace["coarse_lse"] = lse_all
         st.coarse_lse = lse_all
         st.refreshed_at = self.step
         st.valid = True
@@ -299,19 +337,22 @@ class BlockOracle:
         q, k, v = (_rd(t, dt) for t in (q, k, v))
         banks, _, d = q.shape
         scale = 1.0 / math.sqrt(d)
+        self.trace = {}
         q_r, k_r, v_r = self._reorder(q), self._reorder(k), self._reorder(v)
         ctx = self._context(q_r, k_r, v_r, None, scale)
         kmask = self._kernel_mask(st.partition)
         video = self._video_blocks()
         lse_all = torch.empty(banks, self.rows)
+        margin = torch.empty(banks, self.rows, dtype=torch.float64)
         coarse = []
         for b in range(banks):
             drift = {qb: self._drift_rows(ctx, q_r, b, qb, scale) for qb in video}
-            lse_b, outs = self._coarse_bank(b, ctx, q_r, st.partition, scale, video, drift)
+            lse_b, outs, margin[b] = self._coarse_bank(b, ctx, q_r, st.partition, scale, video, drift)
             lse_all[b] = lse_b
             coarse.append(outs)
+        self._note_margin(margin)
         center = orc.drift_center(lse_all, st.coarse_lse)
-        self.trace = dict(center=center, coarse_lse=lse_all)
+        self.trace.update(center=center, coarse_lse=lse_all)
         out = {}
         for qb in self.qblocks:
             rows_b = []
@@ -372,6 +413,19 @@ def sample_qblocks(n_video: int, seq: int, n_video_blocks: int, seed: int = 0) -
     picks = set(np.linspace(0, max(nq - 1, 0), max(1, min(n_video_blocks, nq))).round().astype(int).tolist())
     picks.update(range(nq, NB))  # partial video block and text blocks
     return sorted(picks)
+
+
+def bf16_ulp(x: torch.Tensor) -> torch.Tensor:
+    """One bf16 ulp at magnitude |x| (2^(floor(log2 |x|) - 7))."""
+    m = x.abs().float()
+    return torch.where(m > 0, torch.exp2(torch.floor(torch.log2(m.clamp_min(1e-30))) - 7), torch.zeros_like(m))
+
+
+def chain_bound(exp_rows: torch.Tensor, ulps: float) -> torch.Tensor:
+    """Elementwise bound for outputs assembled from bf16-rounded values: max(2e-2, ``ulps``
+    bf16 ulps of the largest magnitude in the element's row).  ``exp_rows`` [..., rows, d]."""
+    row_max = exp_rows.float().abs().amax(-1, keepdim=True)
+    return torch.clamp(ulps * bf16_ulp(row_max), min=2e-2).expand_as(exp_rows)
 
 
 def compare_bf16(got: torch.Tensor, exp: torch.Tensor) -> dict:

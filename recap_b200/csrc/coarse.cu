@@ -84,17 +84,26 @@ struct CoarseSmem {
   static constexpr int kSums = kXchg + 2 * 2 * 128 * 4;  // (l, g) per half [2][2][128], then T partials [128]
   static constexpr int kBars = kSums + (2 * 2 * 128 + 128) * 4;
   // pro_full, pro_mma, qsq_ready, kw_full[2], kw_empty[2], v_full[2], v_empty[2],
-  // s1full[2], s2full, s2free, pfull, ofull, c_full, xfull, done, xsum, xchg[2 slots][4 quarters]
-  static constexpr int kNumBars = 3 + 8 + 2 + 7 + 1 + 8;
+  // s1full[2], s2full, s2free, pfull[2], ofull, c_full, xfull, done, xsum, xchg[2 slots][4 quarters],
+  // ofin
+  static constexpr int kNumBars = 3 + 8 + 2 + 2 + 6 + 1 + 8 + 1;
   static constexpr int kMisc = kBars + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16 + 4 * 4;
   static_assert(kOpV >= D * D * 2, "U^T is staged in a vbar^T slot");
   static_assert(kKW >= D * D * 2, "C_vk is staged in a (kbar, w) slot");
 };
 
+// Phase discipline: a waiter tests an mbarrier phase by its parity, which tells the current
+// phase from the one before it only; a wait is sound only where the waiter can never be
+// two phases behind the barrier.  So a barrier that completes once per tile is waited on
+// only by a role that cannot fall two tiles behind it, and the epilogue's wait for the
+// last P.V has its own single-phase barrier (ofin): ofull completes once per P.V, and
+// the last two P.V can still run when the epilogue starts.  pfull is double-buffered by
+// the S1 buffer holding P: the softmax arrives on pfull[j & 1] for tile j + 2 only after
+// S1(j + 2), which the MMA warp issues after it has waited for pfull[j & 1] of tile j.
 struct CoarseBars {
   uint64_t *pro_full, *pro_mma, *qsq_ready, *kw_full, *kw_empty, *v_full, *v_empty, *s1full, *s2full, *s2free,
-      *pfull, *ofull, *c_full, *xfull, *done, *xchg, *xsum;
+      *pfull, *ofull, *c_full, *xfull, *done, *xchg, *xsum, *ofin;
 };
 
 __device__ __forceinline__ CoarseBars carve(uint8_t* base) {
@@ -110,13 +119,14 @@ __device__ __forceinline__ CoarseBars carve(uint8_t* base) {
   r.s1full = b + 11;
   r.s2full = b + 13;
   r.s2free = b + 14;
-  r.pfull = b + 15;
-  r.ofull = b + 16;
-  r.c_full = b + 17;
-  r.xfull = b + 18;
-  r.done = b + 19;
-  r.xsum = b + 20;
-  r.xchg = b + 21;  // [slot * 4 + lane quarter]
+  r.pfull = b + 15;  // [S1 buffer]
+  r.ofull = b + 17;
+  r.c_full = b + 18;
+  r.xfull = b + 19;
+  r.done = b + 20;
+  r.xsum = b + 21;
+  r.xchg = b + 22;  // [slot * 4 + lane quarter]
+  r.ofin = b + 30;
   return r;
 }
 
@@ -168,6 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bars.s2full, 1);
     mbar_init(bars.s2free, 8);
     mbar_init(bars.pfull, 8);
+    mbar_init(bars.pfull + 1, 8);
+    mbar_init(bars.ofin, 1);
     for (int i = 0; i < 8; ++i) mbar_init(bars.xchg + i, 2);  // the two warps of a lane quarter
     mbar_init(bars.xsum, 8);
     mbar_init(bars.ofull, 1);
@@ -357,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        if (!wait(bars.pfull, j & 1, kStatusTimeoutMma)) return false;
+        if (!wait(bars.pfull + (j & 1), (j >> 1) & 1, kStatusTimeoutMma)) return false;
         const int st = j % VS;
         if (!wait(bars.v_full + st, (j / VS) & 1, kStatusTimeoutTma)) return false;
         tc_fence_after();
@@ -373,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_bf16_ts_w(leader, t_o, pa, sdesc_k_sw128(vb + offv), idesc, (j > 0 || s > 0) ? 1u : 0u);
         }
         mma_commit_w(leader, bars.ofull);
+        if (j == n_tiles - 1) mma_commit_w(leader, bars.ofin);  // O complete
         mma_commit_w(leader, bars.v_empty + st);
         return true;
       };
@@ -639,7 +652,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // O must hold P.V(j-1) before it is rescaled; P.V(j) starts after pfull below
+      // O must hold P.V(j-1) before it is rescaled; P.V(j) starts after pfull below.  The
+      // parity wait is sound: S1(j), waited for above, was committed after P.V(j-2), so
+      // ofull is at phase j-1 or j here.
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
         ok = wait_all(bars.ofull, (j - 1) & 1);
         if (!ok) break;
@@ -683,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bars.pfull);
+      if (lane == 0) mbar_arrive(bars.pfull + b);
       l_run = l_run * alpha + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
       g_run = g_run * alpha + ((gs[0] + gs[1]) + (gs[2] + gs[3]));
     }
@@ -701,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (ok) {
-      ok = wait_all(bars.ofull, (n_tiles - 1) & 1);
+      ok = wait_all(bars.ofin, 0);  // every P.V has completed (ofull may be two phases ahead)
       if (ok) ok = wait_all(bars.xfull, 0);
     }
     if (ok) {

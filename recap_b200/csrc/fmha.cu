@@ -60,8 +60,8 @@ struct FmhaSmem {
   static constexpr int kQ = 0;                        // Q_A, Q_B
   static constexpr int kKV = kQ + 2 * kTileBytes;     // ring of K / V^T tiles
   static constexpr int kBars = kKV + kNst * kTileBytes;
-  // qfull, full[NST], empty[NST], sfull[2], pfull[2], ofin[2], done
-  static constexpr int kNumBars = 1 + 2 * kNst + 7;
+  // qfull, full[NST], empty[NST], sfull[2], pfull[2], ofin[2], done, efull[2]
+  static constexpr int kNumBars = 1 + 2 * kNst + 9;
   static constexpr int kMisc = kBars + kNumBars * 8;  // tmem base, abort flag, LA, LB, nS
   static constexpr int kList = kMisc + 32;            // uint16 list_a[2048], only_b[2048]
   static constexpr int kRows = kList + 2 * kMaxKeyBlocks * 2;  // staged partition rows, 2 x 2048 bytes
@@ -69,8 +69,14 @@ struct FmhaSmem {
   static constexpr int kTotal = kCounts + 3 * (kThreads / 32) * 4;
 };
 
+// Phase discipline: an mbarrier phase is tested by its parity, which tells the current
+// phase from the one before it only, so every wait below is by a role that cannot be two
+// phases behind the barrier.  The epilogue tiles of a merged query block land in ring slots
+// but complete on their own single-phase barrier efull[tile]: they are loaded after the
+// whole walk, which for a pair of very unequal tiles (a block keeping every key block next
+// to one keeping a tenth) is hundreds of slot phases after the epilogue's tile finished.
 struct Bars {
-  uint64_t *qfull, *full, *empty, *sfull, *pfull, *ofin, *done;
+  uint64_t *qfull, *full, *empty, *sfull, *pfull, *ofin, *done, *efull;
 };
 
 template <int NST>
@@ -84,6 +90,7 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* base) {
   r.pfull = b + 3 + 2 * NST;
   r.ofin = b + 5 + 2 * NST;
   r.done = b + 7 + 2 * NST;
+  r.efull = b + 8 + 2 * NST;
   return r;
 }
 
@@ -214,6 +221,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bars.ofin + x, 1);
     }
     mbar_init(bars.done, 1);
+    mbar_init(bars.efull, 1);
+    mbar_init(bars.efull + 1, 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tm_q);
@@ -351,7 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       });
       // The epilogue's coarse output and refinement tiles (one 128-row tile of each per
       // merged query block) go into the ring slots as they come free, as loads number
-      // n_own, n_own + 1, ... after the walk's n_own loads.
+      // n_own, n_own + 1, ... after the walk's n_own loads; they complete on efull[tile].
+      const int n_walk = load_no;
+      bool e_issued[2] = {false, false};
       if (args.tma_epilogue && !*abort_flag) {
         const uint64_t stream = l2_evict_first();  // read once
 #pragma unroll 1
@@ -359,20 +370,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int qblock = y == 0 ? it.qa : it.qb;
           if (qblock < 0 || (qblock + 1) * 128 > args.rows) continue;
           const int row0 = it.bank * args.rows + qblock * 128;
+          bool ok_y = true;
 #pragma unroll 1
-          for (int k = 0; k < 2; ++k) {
+          for (int k = 0; k < 2 && ok_y; ++k) {
             const int slot = load_no % NST;
             if (load_no >= NST &&
                 !mbar_wait(bars.empty + slot, ((load_no / NST) - 1) & 1, abort_flag, args.status,
-                           kStatusTimeoutProducer))
+                           kStatusTimeoutProducer)) {
+              ok_y = false;
               break;
+            }
             uint8_t* dst = sKV + slot * kTileBytes;
-            mbar_expect_tx(bars.full + slot, kTileBytes);
+            if (k == 0) {
+              mbar_expect_tx(bars.efull + y, 2 * kTileBytes);
+              e_issued[y] = true;
+            }
 #pragma unroll
             for (int a = 0; a < D / 64; ++a)
-              tma_load_2d_hint(dst + a * 128 * 128, k == 0 ? &tm_go : &tm_det, bars.full + slot, a * 64, row0, stream);
+              tma_load_2d_hint(dst + a * 128 * 128, k == 0 ? &tm_go : &tm_det, bars.efull + y, a * 64, row0, stream);
             ++load_no;
           }
+          if (!ok_y) break;
         }
       }
       // The CTA that starts when this one ends is about blockIdx.x + the number of SMs: put
@@ -400,8 +418,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Leave no bulk copy in flight: wait for the last loads this thread issued.
-      const int first = load_no > NST ? load_no - NST : 0;
-      for (int k = first; k < load_no; ++k) mbar_drain(bars.full + (k % NST), (k / NST) & 1);
+      const int first = n_walk > NST ? n_walk - NST : 0;
+      for (int k = first; k < n_walk; ++k) mbar_drain(bars.full + (k % NST), (k / NST) & 1);
+      for (int y = 0; y < 2; ++y)
+        if (e_issued[y]) mbar_drain(bars.efull + y, 0);
     }
     if (lane == 0) mbar_drain(bars.qfull, 0);
   } else if (warp == 1) {
@@ -621,9 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok && staged) {
-      ok = mbar_wait(bars.full + n_go % NST, (n_go / NST) & 1, abort_flag, args.status, kStatusTimeoutSoftmax) &&
-           mbar_wait(bars.full + (n_go + 1) % NST, ((n_go + 1) / NST) & 1, abort_flag, args.status,
-                     kStatusTimeoutSoftmax);
+      ok = mbar_wait(bars.efull + x, 0, abort_flag, args.status, kStatusTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {

@@ -284,7 +284,7 @@ class SparseAttention:
             )
             symmetric = 0.5 * (scatter + scatter.transpose(-1, -2))
             _, evecs = torch.linalg.eigh(symmetric)
-            evecs = evecs.contiguous()
+            evecs = _orthonormalize(evecs)
             unsorted, _ = full_variance(evecs, 0)
             counts = self.geometry.block_counts.to(dev).reshape(1, -1, 1)
             pooled = (unsorted * counts).sum(1) / counts.sum().clamp_min(1.0)
@@ -349,6 +349,20 @@ class SparseAttention:
             _lib.stream_handle(dev),
         )
         return out, lse, center
+
+
+def _orthonormalize(u: torch.Tensor) -> torch.Tensor:
+    """The eigenvectors of an fp32 eigh are orthonormal only to ~3e-5.  The layout pass
+    takes the folded tail of the per-block variances from the trace identity
+    sum_c var(K U[:, c]) = trace(cov K), which holds for an orthonormal U: two Newton-Schulz
+    steps in fp64 (U <- U (3 I - U^T U) / 2, quadratic convergence from 3e-5) make U
+    orthonormal to fp32 rounding, moving each vector by ~1e-5, well inside the freedom
+    eigh leaves it (signs, rotations within near-degenerate eigenspaces)."""
+    x = u.double()
+    eye3 = 3.0 * torch.eye(x.shape[-1], dtype=x.dtype, device=x.device)
+    for _ in range(2):
+        x = 0.5 * x @ (eye3 - x.transpose(-1, -2) @ x)
+    return x.float().contiguous()
 
 
 def _strides3(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):

@@ -188,12 +188,12 @@ def test_exact_matches_dense_attention():
     assert float((out - ref).abs().max()) <= MAX_ABS
 
 
-@pytest.mark.parametrize("prefetch", [True, False])
-def test_host_bank_streaming_matches_resident(prefetch):
+@pytest.mark.parametrize("prefetch,slots", [(True, 2), (False, 1), (True, 3)])
+def test_host_bank_streaming_matches_resident(prefetch, slots):
     """HostBankOperator with an HBM budget of zero streams each layer's refinement through
-    pinned host memory (two device slots, prefetch and write-back streams); its outputs
-    equal the HBM-resident operator's bit for bit over refresh -> sparse -> sparse ->
-    refresh across three layers (the copies are exact and the kernels are the same)."""
+    pinned host memory (a ring of device slots, prefetch and write-back streams); its
+    outputs equal the HBM-resident operator's bit for bit over refresh -> sparse -> sparse
+    -> refresh across three layers (the copies are exact and the kernels are the same)."""
     from recap_b200 import REFRESH, SPARSE, HostBankOperator, Operator, OperatorConfig
     from recap_b200.sparse import Layout, SparseGeometry, hilbert_permutation
 
@@ -206,6 +206,7 @@ def test_host_bank_streaming_matches_resident(prefetch):
     resident = Operator.build(cfg, geo, n_layers=n_layers)
     streamed = HostBankOperator.build(cfg, geo, n_layers=n_layers)
     streamed.hbm_budget = 0
+    streamed.ring_slots = slots
     streamed.set_prefetch(prefetch)
     held = streamed.preallocate_host(n_layers, spec["heads"], spec["dim"])
     assert streamed.resident is False and held > 0
