@@ -28,10 +28,34 @@ import torch
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-WORKLOAD = dict(name="hunyuan720p_layer", grid=(33, 45, 80), heads=24, dim=128, text=256, text_first=False,
-                density=0.1)
-METRIC = "corrected sparse-attn us/layer call (HunyuanVideo-720p layer, SPARSE step)"
+# BASELINE configs 4 (the headline), 2 and 3.  batch: the layer call's batch (CogVideoX runs
+# its two guidance branches as batch 2, recap/models/cogvideox.py:17).
+WORKLOADS = {
+    "hunyuan720p_layer": dict(name="hunyuan720p_layer", label="HunyuanVideo-720p layer", grid=(33, 45, 80),
+                              heads=24, dim=128, text=256, text_first=False, density=0.1, batch=1),
+    "wan480p_layer": dict(name="wan480p_layer", label="Wan2.1-1.3B 480p layer", grid=(21, 30, 52), heads=12,
+                          dim=128, text=0, text_first=False, density=0.2, batch=1),
+    "cogvideox768_layer": dict(name="cogvideox768_layer", label="CogVideoX-1.5 768p layer, guidance batch 2",
+                               grid=(11, 48, 85), heads=48, dim=64, text=226, text_first=True, density=0.15,
+                               batch=2),
+}
+WORKLOAD = WORKLOADS["hunyuan720p_layer"]
 UNIT = "us/layer"
+
+
+def metric_of(w: dict) -> str:
+    return f"corrected sparse-attn us/layer call ({w['label']}, SPARSE step)"
+
+
+METRIC = metric_of(WORKLOAD)
+
+
+def head_slice(heads: int, world: int, rank: int) -> range:
+    """This rank's heads: contiguous, the first heads % world ranks one more (12 heads over
+    8 GPUs: 2/2/2/2/1/1/1/1)."""
+    base, extra = divmod(heads, world)
+    lo = rank * base + min(rank, extra)
+    return range(lo, lo + base + (1 if rank < extra else 0))
 
 
 def parse():
@@ -40,6 +64,8 @@ def parse():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default=WORKLOAD["name"],
+                   help="BASELINE config 4 (default), 2 or 3")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true", help="skip the CPU oracle check of the last timed output")
@@ -53,10 +79,10 @@ def parse():
 
 
 def synth_qkv(grid, heads: range, dim: int, text: int, text_first: bool, seed: int, device, rank: int = 16,
-              noise: float = 0.5):
-    """Seeded Q/K/V [1, len(heads), S, dim] bf16 with per-frame spatially smooth low-rank
+              noise: float = 0.5, batch: int = 1):
+    """Seeded Q/K/V [batch, len(heads), S, dim] bf16 with per-frame spatially smooth low-rank
     structure (sum of 4 low-frequency cosines per factor, per-frame phase drift) plus
-    noise; text tokens N(0,1).  Generated per head on the device."""
+    noise; text tokens N(0,1).  Generated per (batch, head) on the device."""
     T, H, W = grid
     nv = T * H * W
     tt = torch.arange(T, dtype=torch.float32, device=device).view(T, 1, 1)
@@ -64,9 +90,9 @@ def synth_qkv(grid, heads: range, dim: int, text: int, text_first: bool, seed: i
     xx = (torch.arange(W, dtype=torch.float32, device=device) / W).view(1, 1, W)
     out = []
     for tensor in range(3):
-        x = torch.empty(1, len(heads), nv + text, dim, dtype=torch.bfloat16, device=device)
-        for i, h in enumerate(heads):
-            g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + tensor * 10_007 + h)
+        x = torch.empty(batch, len(heads), nv + text, dim, dtype=torch.bfloat16, device=device)
+        for bi, i, h in ((bi, i, h) for bi in range(batch) for i, h in enumerate(heads)):
+            g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + tensor * 10_007 + h + 100_003 * bi)
             u = torch.randn(rank, dim, generator=g, device=device) / math.sqrt(rank)
             amp = torch.randn(rank, 4, generator=g, device=device)
             ky = torch.randint(-2, 3, (rank, 4), generator=g, device=device).float()
@@ -79,7 +105,7 @@ def synth_qkv(grid, heads: range, dim: int, text: int, text_first: bool, seed: i
                 f += v(amp) * torch.cos(2 * math.pi * (v(ky) * yy + v(kx) * xx) + v(ph) + v(dr) * tt)
             vid = f.reshape(rank, nv).T @ u + noise * torch.randn(nv, dim, generator=g, device=device)
             txt = torch.randn(text, dim, generator=g, device=device)
-            x[0, i] = torch.cat([txt, vid]) if text_first else torch.cat([vid, txt])
+            x[bi, i] = torch.cat([txt, vid]) if text_first else torch.cat([vid, txt])
         out.append(x)
     return out
 
@@ -237,7 +263,7 @@ def traffic_per_launch() -> float | None:
         return None
 
 
-def end_to_end(op, host, steps: int, group, world: int, n_heads: int, S: int, d: int) -> dict:
+def end_to_end(op, host, steps: int, group, n_heads: int, total_heads: int) -> dict:
     """The layer call through ``Operator.attend`` with host-resident inputs and outputs:
     every step copies its Q/K/V from pinned host memory to the device and its output back.
     Double-buffered like a serving loop: the host-to-device copy of step i+1 and the
@@ -253,7 +279,7 @@ def end_to_end(op, host, steps: int, group, world: int, n_heads: int, S: int, d:
     h2d_s = [torch.cuda.Stream() for _ in host[0]]
     d2h_s = torch.cuda.Stream()
     dev_in = [[torch.empty_like(t, device=dev) for t in host[0]] for _ in range(2)]
-    out_host = [torch.empty(1, n_heads, S, d, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    out_host = [torch.empty(host[0][0].shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
 
     def timed(fn) -> float:
         torch.cuda.synchronize()
@@ -315,9 +341,11 @@ def end_to_end(op, host, steps: int, group, world: int, n_heads: int, S: int, d:
     torch.cuda.synchronize()
     t_serial = timed(serial)
     t_pipe = timed(pipelined)
-    h2d = sum(t.numel() * t.element_size() for t in host[0])
-    return {"value": round(t_pipe, 1), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
-            "d2h_bytes_per_step": out_host[0].numel() * 2 * world,
+    # bytes of all ranks: this rank's per head, times the layer's heads
+    h2d = sum(t.numel() * t.element_size() for t in host[0]) // n_heads * total_heads
+    d2h = out_host[0].numel() * 2 // n_heads * total_heads
+    return {"value": round(t_pipe, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
             "pipeline": "double-buffered: H2D of step i+1 (one copy stream per input tensor) and D2H of step i on copy streams during step i",
             "serial_value": round(t_serial, 1)}
 
@@ -326,10 +354,14 @@ def workload_config(w: dict, world: int) -> dict:
     """The ``config`` of both arms' JSON lines."""
     nv = w["grid"][0] * w["grid"][1] * w["grid"][2]
     nb = (nv + 127) // 128
-    return {"workload": w["name"], "heads": w["heads"], "head_dim": w["dim"], "video_tokens": nv,
-            "text_tokens": w["text"], "seq_len": nv + w["text"], "key_blocks": nb,
-            "keep": max(1, round(w["density"] * nb)), "parallelism": f"heads/{world}", "bank": "HBM",
-            "l2": "inputs 2.19 GB per step > 126 MB L2 (no flush needed)"}
+    S = nv + w["text"]
+    in_gb = 3 * w["batch"] * w["heads"] * S * w["dim"] * 2 / 1e9
+    split = [len(head_slice(w["heads"], world, r)) for r in range(world)]
+    par = f"heads/{world}" if len(set(split)) == 1 else f"heads/{world} uneven " + "/".join(map(str, split))
+    return {"workload": w["name"], "batch": w["batch"], "heads": w["heads"], "head_dim": w["dim"],
+            "video_tokens": nv, "text_tokens": w["text"], "seq_len": S, "key_blocks": nb,
+            "keep": max(1, round(w["density"] * nb)), "parallelism": par, "bank": "HBM",
+            "l2": f"inputs {in_gb:.2f} GB per step > 126 MB L2 (no flush needed)"}
 
 
 def parity_leg(w: dict, layout, hx: dict, basis, part0, part2, keep: bool, out_rows: dict, oracle_qblocks) -> dict:
@@ -385,14 +417,14 @@ def run_ours(args) -> None:
 
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
         group = dist.group.WORLD
-    w = dict(WORKLOAD)
+    w = dict(WORKLOADS[args.workload])
     if args.heads:
         w["heads"] = int(args.heads)
         w["name"] = f'{w["name"]}_{args.heads}heads'
     H = w["heads"]
-    if H % world:
-        raise SystemExit(f"{H} heads do not split over {world} GPUs")
-    hs = range(rank * H // world, (rank + 1) * H // world)
+    if H < world:
+        raise SystemExit(f"{H} heads cannot give each of {world} GPUs one")
+    hs = head_slice(H, world, rank)
     perm = hilbert_permutation(w["grid"])
     layout = Layout.from_permutation(perm, text_tokens=w["text"], text_first=w["text_first"])
     geo = SparseGeometry.build(layout, 128)
@@ -402,7 +434,7 @@ def run_ours(args) -> None:
     S = nv + w["text"]
     d = w["dim"]
 
-    x0 = synth_qkv(w["grid"], hs, d, w["text"], w["text_first"], seed=0, device=dev)
+    x0 = synth_qkv(w["grid"], hs, d, w["text"], w["text_first"], seed=0, device=dev, batch=w["batch"])
     op.begin_step(0, REFRESH)
     op.attend(0, *x0)
     torch.cuda.synchronize()
@@ -425,6 +457,10 @@ def run_ours(args) -> None:
     op.begin_step(1, REFRESH)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    if group is not None:
+        # the revalidating refresh all-reduces its overlap counts: have NCCL set up the
+        # int64 all-reduce before the timed region
+        dist.all_reduce(torch.zeros(2, dtype=torch.int64, device=dev), group=group)
     torch.cuda.synchronize()
     if group is not None:
         dist.barrier(group=group)
@@ -496,13 +532,14 @@ def run_ours(args) -> None:
     achieved = flops / (fmha_ms * 1e-3) / 1e12 if fmha_ms else None
     traffic = traffic_per_launch()
     if traffic is not None:
-        traffic = traffic * len(hs) / WORKLOAD["heads"]  # the committed figure is for all 24 heads on one GPU
+        # the committed figure is for all 24 heads of the default workload on one GPU
+        traffic = traffic * len(hs) / WORKLOAD["heads"] if w["name"] == WORKLOAD["name"] else None
 
     # end to end through the API with host buffers
     e2e = None
     if not args.no_e2e:
         host = [[t.cpu().pin_memory() for t in xs] for xs in inputs]
-        e2e = end_to_end(op, host, args.steps, group, world, len(hs), S, d)
+        e2e = end_to_end(op, host, args.steps, group, len(hs), H)
         del host
     op.check_device_status()
 
@@ -518,9 +555,9 @@ def run_ours(args) -> None:
         cpu = time_sparse_sample(op, inputs[0], layout, w)
 
     if rank == 0:
-        dense_flops = 4.0 * S * S * d * H
+        dense_flops = 4.0 * S * S * d * H * w["batch"]
         line = {
-            "metric": METRIC, "value": round(ms_per_step * 1000.0, 1), "unit": UNIT, "n_gpus": world,
+            "metric": metric_of(w), "value": round(ms_per_step * 1000.0, 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded smooth low-rank (rank 16) + 0.5 noise Q/K/V, 0.05 perturbation per step",
@@ -561,8 +598,9 @@ def run_reference(args) -> None:
         return
     from oracle.cpu_baseline import reference_arm
 
-    line = reference_arm(WORKLOAD, METRIC, UNIT, steps=args.steps, warmup=args.warmup,
-                         config=workload_config(WORKLOAD, world))
+    w = WORKLOADS[args.workload]
+    line = reference_arm(w, metric_of(w), UNIT, steps=args.steps, warmup=args.warmup,
+                         config=workload_config(w, world))
     line.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup})
     print(json.dumps(line), flush=True)
 

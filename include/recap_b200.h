@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define RECAP_B200_ABI_VERSION 6
+#define RECAP_B200_ABI_VERSION 7
 
 #define RECAP_OK 0
 #define RECAP_ERR_SHAPE 1
@@ -169,6 +169,22 @@ int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, co
                             const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
                             int n_video, int all_blocks, float scale, const int32_t* out_pos, void* out,
                             float* lse, int* status, void* stream);
+
+/* The two attentions of a REFRESH in one pass: dense attention over every key block and,
+ * on the way, the block-sparse head over the partition's kept blocks.  Replaces the dense
+ * aten._scaled_dot_product_flash_attention of recap/operator.py:254-256 together with the
+ * block_sparse_exact head of recap/operator.py:366-373 (recap/kernels/block_sparse.py:78-139).
+ * Each query block walks its kept key blocks first, in the order the block-sparse pass
+ * takes them, writes the head output and LSE, then walks the omitted blocks to the dense
+ * result.  The head equals recap_block_sparse_fmha's (all_blocks = 0, out_pos NULL, the same
+ * k_norm_max) bit for bit: the same kept blocks in the same order and the same arithmetic.
+ *   out / lse           [banks, S, D] bf16 / [banks, S] fp32 dense result, reordered row r at
+ *                       row out_pos[r] (out_pos NULL: row r)
+ *   head_out / head_lse [banks, S, D] bf16 / [banks, S] fp32 head result, reordered order */
+int recap_refresh_attention(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                            const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
+                            int n_video, float scale, const int32_t* out_pos, void* out, float* lse,
+                            void* head_out, float* head_lse, int* status, void* stream);
 
 /* The corrected SPARSE step: block-sparse attention with the drift-weighted merge of the coarse
  * tail and the cached refinement fused as its epilogue, written in native order.

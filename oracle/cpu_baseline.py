@@ -236,7 +236,8 @@ class FullLayer:
         self.nB = (self.nv + BLOCK - 1) // BLOCK
         self.NB = (self.S + BLOCK - 1) // BLOCK
         self.rows = (self.nv // BLOCK) * BLOCK
-        self.heads = spec["heads"] if heads is None else int(heads)
+        # banks of the layer call: heads x batch (a batch's banks draw further head indices)
+        self.heads = spec["heads"] * spec.get("batch", 1) if heads is None else int(heads)
         self.seed = seed
         self.fwd, self.inv = orc.gather_indices(torch.as_tensor(self.perm), self.text, self.text_first)
         torch.set_num_threads(host_threads())
@@ -244,7 +245,7 @@ class FullLayer:
         self.inputs: list[tuple] = []
 
     def _bank_inputs(self, h: int):
-        x0 = [t[0, 0] for t in orc.smooth_lowrank(self.spec["grid"], self.spec["heads"], self.d, self.text,
+        x0 = [t[0, 0] for t in orc.smooth_lowrank(self.spec["grid"], max(self.spec["heads"], h + 1), self.d, self.text,
                                                    self.text_first, self.seed, head_slice=slice(h, h + 1))]
         x1 = [orc.perturb_heads(t[None, None], seed=1, tensor=i, head_offset=h)[0, 0] for i, t in enumerate(x0)]
         return x0, x1
@@ -358,9 +359,11 @@ def time_sparse_sample(op=None, inputs=None, layout=None, spec=None, repeats: in
     runner = SampledLayer(spec)
     runner.refresh()
     runner.step()  # warm-up
-    vals = sorted(runner.layer_us(runner.step(), spec["heads"]) for _ in range(repeats))
+    banks = spec["heads"] * spec.get("batch", 1)
+    vals = sorted(runner.layer_us(runner.step(), banks) for _ in range(repeats))
+    sample = runner.sample_text() + (f"; x{spec['batch']} for the layer's batch" if spec.get("batch", 1) > 1 else "")
     return {"value": round(vals[len(vals) // 2], 1), "unit": "us/layer", "cores": host_threads(),
-            "torch_threads": torch.get_num_threads(), "kind": "port", "sample": runner.sample_text()}
+            "torch_threads": torch.get_num_threads(), "kind": "port", "sample": sample}
 
 
 def reference_arm(spec: dict, metric: str, unit: str, steps: int, warmup: int, config: dict | None = None) -> dict:
@@ -376,7 +379,7 @@ def reference_arm(spec: dict, metric: str, unit: str, steps: int, warmup: int, c
     runner.refresh()
     for _ in range(max(1, warmup)):
         runner.step()
-    est = sorted(runner.layer_us(runner.step(), spec["heads"]) for _ in range(2))
+    est = sorted(runner.layer_us(runner.step(), spec["heads"] * spec.get("batch", 1)) for _ in range(2))
     sampled = est[len(est) // 2]
     full = FullLayer(spec)
     t_setup = time.perf_counter()

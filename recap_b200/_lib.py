@@ -16,7 +16,7 @@ import torch
 PACKAGE_DIR = Path(__file__).resolve().parent
 LIB_PATH = PACKAGE_DIR / "librecap_b200.so"
 
-ABI_VERSION = 6  # RECAP_B200_ABI_VERSION of include/recap_b200.h
+ABI_VERSION = 7  # RECAP_B200_ABI_VERSION of include/recap_b200.h
 
 RECAP_OK = 0
 RECAP_ERR_SHAPE = 1
@@ -55,6 +55,7 @@ SIGNATURES: dict[str, tuple] = {
     "recap_coarse_tail": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _I, _P, _P, _P, _P,
                                _P, _P]),
     "recap_block_sparse_fmha": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P]),
+    "recap_refresh_attention": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P]),
     "recap_sparse_step": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "recap_refresh_partials": (_I, [_I, _I]),
     "recap_refresh_detail": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),

@@ -319,6 +319,41 @@ int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, co
   return launch_fmha(L, static_cast<cudaStream_t>(stream));
 }
 
+int recap_refresh_attention(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                            const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
+                            int n_video, float scale, const int32_t* out_pos, void* out, float* lse,
+                            void* head_out, float* head_lse, int* status, void* stream) {
+  Geom g;
+  if (!geom(S, n_video, &g) || !d_ok(D) || banks <= 0 || out == nullptr || lse == nullptr ||
+      partition == nullptr || head_out == nullptr || head_lse == nullptr)
+    return kErrShape;
+  FmhaLaunch L{};
+  L.D = D;
+  int rc = fmha_common(q_reordered, k_reordered, v_transposed, banks, S, D, &L);
+  if (rc != kOk) return rc;
+  FmhaArgs& a = L.args;
+  a.banks = banks;
+  a.S = S;
+  a.S_pad = g.S_pad;
+  a.NB = g.NB;
+  a.nB = g.nB;
+  a.dense_start = g.dense_start;
+  a.rows = g.rows;
+  a.all_blocks = 1;
+  a.refresh = 1;
+  a.head_o = static_cast<__nv_bfloat16*>(head_out);
+  a.head_lse = head_lse;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.partition = partition;
+  a.k_norm_max = k_norm_max;
+  a.epilogue = 0;
+  a.out_pos = out_pos;
+  a.o = static_cast<__nv_bfloat16*>(out);
+  a.lse = lse;
+  a.status = status;
+  return launch_fmha(L, static_cast<cudaStream_t>(stream));
+}
+
 int recap_sparse_step(const void* q_reordered, const void* k_reordered, const void* v_transposed,
                       const uint8_t* partition, const float* k_norm_max, int banks, int S, int D, int n_video,
                       float scale,

@@ -31,6 +31,15 @@
 // recap/kernels/detail_cache.py:188-301 (drift-weighted refinement + coarse tail,
 // merged in log-mass space) and writes the result straight to the native token
 // order (the Layout.restore gather of recap/sparse/layout.py:90-92).
+//
+// Refresh mode (recap/operator.py:253-258 and 366-373: the dense flash call and the
+// block-sparse head over the same Q, K, V): every key block, with each tile's kept
+// blocks first, in the order the sparse step walks them.  When a tile's softmax reaches
+// its first omitted block, O holds exactly the kept blocks' products, so that tile's
+// head output and LSE are written then (the same arithmetic and order as the head-only
+// pass, so the same bits); the walk goes on over the omitted blocks to the dense result.
+// Lists: A = [both keep | A only | B only | neither], B = [both | B only | A only |
+// neither], so the first and last parts share their K / V^T tiles.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -62,7 +71,7 @@ struct FmhaSmem {
   static constexpr int kBars = kKV + kNst * kTileBytes;
   // qfull, full[NST], empty[NST], sfull[2], pfull[2], ofin[2], done, efull[2]
   static constexpr int kNumBars = 1 + 2 * kNst + 9;
-  static constexpr int kMisc = kBars + kNumBars * 8;  // tmem base, abort flag, LA, LB, nS
+  static constexpr int kMisc = kBars + kNumBars * 8;  // tmem base, abort flag, LA, LB, nS, kept A, kept B
   static constexpr int kList = kMisc + 32;            // uint16 list_a[2048], only_b[2048]
   static constexpr int kRows = kList + 2 * kMaxKeyBlocks * 2;  // staged partition rows, 2 x 2048 bytes
   static constexpr int kCounts = kRows + 2 * kMaxKeyBlocks;   // per-warp list counts [warps][3]
@@ -158,7 +167,7 @@ __device__ __forceinline__ bool walk_ops(int LA, int LB, Op&& op) {
   return true;
 }
 
-template <int D>
+template <int D, bool kRefresh>
 __global__ void __launch_bounds__(kThreads, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_vt, const __grid_constant__ CUtensorMap tm_go,
@@ -187,8 +196,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const Item it = decode_item(args, blockIdx.x);
   const int NB = args.NB;
   const bool has_b = it.qb >= 0;
-  const bool dense_a = args.all_blocks || it.qa >= args.dense_start;
-  const bool dense_b = args.all_blocks || (has_b && it.qb >= args.dense_start);
+  constexpr bool refresh = kRefresh;  // a template parameter: the sparse-step code is unchanged
+  const bool every = args.all_blocks && !refresh;  // no partition: every block is kept
+  const bool dense_a = every || it.qa >= args.dense_start;
+  const bool dense_b = every || (has_b && it.qb >= args.dense_start);
 
   // ---- the two partition rows of the key-block lists: every byte load of this thread
   // goes out first, so that their latency overlaps the barrier setup and the TMEM
@@ -260,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     static_assert(8 * kThreads >= kMaxKeyBlocks, "one compaction pass");
     constexpr int kWarps = kThreads / 32;
     const int q = threadIdx.x;
-    uint32_t bs = 0, ba = 0, bb = 0;  // bit e: block 8q + e in the category
+    uint32_t bs = 0, ba = 0, bb = 0, bn = 0;  // bit e: block 8q + e in the category
     if (8 * q < NB) {
       const uint2 wa = reinterpret_cast<const uint2*>(row_a)[q];
       const uint2 wb = reinterpret_cast<const uint2*>(row_b)[q];
@@ -276,10 +287,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         bs |= (ka && kb) ? 1u << e : 0u;
         ba |= (ka && !kb) ? 1u << e : 0u;
         bb |= (kb && !ka) ? 1u << e : 0u;
+        bn |= (refresh && in && !ka && !kb) ? 1u << e : 0u;  // walked after the kept ones
       }
     }
-    // inclusive warp scans of the counts: (shared | A-only << 16) and B-only
-    const uint32_t m1 = __popc(bs) | (__popc(ba) << 16), m2 = __popc(bb);
+    // inclusive warp scans of the counts: (shared | A-only << 16) and (B-only | neither << 16)
+    const uint32_t m1 = __popc(bs) | (__popc(ba) << 16), m2 = __popc(bb) | (__popc(bn) << 16);
     uint32_t i1 = m1, i2 = m2;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -306,19 +318,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       t1 += c1;
       t2 += c2;
     }
-    const int n_shared = t1 & 0xffff, ta = t1 >> 16, tb = t2;
-    int os = b1 & 0xffff, oa = n_shared + (b1 >> 16), ob = b2;
+    const int n_shared = t1 & 0xffff, ta = t1 >> 16, tb = t2 & 0xffff, tn = t2 >> 16;
+    int os = b1 & 0xffff, oa = n_shared + (b1 >> 16), ob = b2 & 0xffff;
+    if (!refresh) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const uint16_t j = static_cast<uint16_t>(8 * q + e);
-      if ((bs >> e) & 1u) list_a[os++] = j;
-      if ((ba >> e) & 1u) list_a[oa++] = j;
-      if ((bb >> e) & 1u) only_b[ob++] = j;
+      for (int e = 0; e < 8; ++e) {
+        const uint16_t j = static_cast<uint16_t>(8 * q + e);
+        if ((bs >> e) & 1u) list_a[os++] = j;
+        if ((ba >> e) & 1u) list_a[oa++] = j;
+        if ((bb >> e) & 1u) only_b[ob++] = j;
+      }
+    } else {
+      // list_a = [shared | A only | B only | neither]; only_b (B's rounds from n_shared on)
+      // = [B only | A only | neither]
+      int oa_b = tb + (b1 >> 16);
+      int ob_a = n_shared + ta + (b2 & 0xffff);
+      int on_a = n_shared + ta + tb + (b2 >> 16);
+      int on_b = tb + ta + (b2 >> 16);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint16_t j = static_cast<uint16_t>(8 * q + e);
+        if ((bs >> e) & 1u) list_a[os++] = j;
+        if ((ba >> e) & 1u) {
+          list_a[oa++] = j;
+          only_b[oa_b++] = j;
+        }
+        if ((bb >> e) & 1u) {
+          only_b[ob++] = j;
+          list_a[ob_a++] = j;
+        }
+        if ((bn >> e) & 1u) {
+          list_a[on_a++] = j;
+          only_b[on_b++] = j;
+        }
+      }
     }
     if (threadIdx.x == 0) {
-      lens[0] = n_shared + ta;
-      lens[1] = has_b ? n_shared + tb : 0;
+      const int all = n_shared + ta + tb + tn;  // refresh: NB
+      lens[0] = refresh ? all : n_shared + ta;
+      lens[1] = has_b ? (refresh ? all : n_shared + tb) : 0;
       lens[2] = n_shared;
+      lens[3] = n_shared + ta;  // kept by A
+      lens[4] = n_shared + tb;  // kept by B
     }
   }
   __syncthreads();
@@ -329,6 +370,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto block_of = [&](int x, int round) -> int {
     return (x == 0 || round < nS) ? list_a[round] : only_b[round - nS];
   };
+  // Whether tile B's op of this round uses the K / V^T tile that tile A's op loaded: the
+  // shared prefix, and in refresh mode every later round whose two blocks coincide (the
+  // blocks neither tile keeps, or all of them when one tile keeps every block).
+  auto shared_round = [&](int round) -> bool {
+    return round < nS || (refresh && LB > 0 && list_a[round] == only_b[round - nS]);
+  };
 
   if (warp == 0) {
     // ================================================================ producer
@@ -336,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t keep = l2_evict_last();  // K and V tiles: re-read by many CTAs
       int load_no = 0;
       walk_ops(LA, LB, [&](int x, int kind, int round) -> bool {
-        if (x == 1 && round < nS) return true;  // the tile-A op of this round loaded it
+        if (x == 1 && shared_round(round)) return true;  // the tile-A op of this round loaded it
         const int slot = load_no % NST;
         if (load_no >= NST &&
             !mbar_wait(bars.empty + slot, ((load_no / NST) - 1) & 1, abort_flag, args.status,
@@ -405,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int qblock = y == 0 ? in.qa : in.qb;
             if (qblock < 0) continue;
             prefetch_l2_bulk(args.q + (static_cast<size_t>(in.bank) * args.S_pad + qblock * 128) * D, kTileBytes);
-            const bool dense_q = args.all_blocks || qblock >= args.dense_start;
+            const bool dense_q = (args.all_blocks && !refresh) || qblock >= args.dense_start;
             if (!dense_q) {
               // the whole 16-byte pieces inside the partition row
               const uintptr_t lo = reinterpret_cast<uintptr_t>(args.partition +
@@ -438,7 +485,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int slot_k = 0, slot_v = 0;  // latest slot of each kind (K for S, V^T for PV)
       if (__all_sync(0xffffffffu, mbar_wait(bars.qfull, 0, abort_flag, args.status, kStatusTimeoutTma))) {
         walk_ops(LA, LB, [&](int x, int kind, int round) -> bool {
-          const bool reuse = x == 1 && round < nS;
+          const bool shared = shared_round(round);
+          const bool reuse = x == 1 && shared;
           int slot;
           if (!reuse) {
             slot = load_no % NST;
@@ -476,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (round == (x == 0 ? LA : LB) - 1) mma_commit_w(leader, bars.ofin + x);
           }
-          if (x == 1 || round >= nS) mma_commit_w(leader, bars.empty + slot);  // last user of the slot
+          if (x == 1 || !shared) mma_commit_w(leader, bars.empty + slot);  // last user of the slot
           return true;
         });
       }
@@ -497,6 +545,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale_log2 = args.scale_log2;
     float m_run = -INFINITY;  // running max, log2 domain (scaled)
     float l_run = 0.f;        // running row sum at m_run
+    // Refresh mode: the round at which O holds exactly this tile's kept blocks (written
+    // before that round's exponentials; == Lx: after the walk, in the epilogue).
+    const int head_round = refresh ? (x == 0 ? lens[3] : lens[4]) : -1;
+    // Head output and LSE of this row from O and the running max / sum (the head-only
+    // pass's epilogue arithmetic).  Warp-collective: the TMEM loads run on every lane.
+    auto write_head = [&](float m_h, float l_h) {
+      const int hr = qblock * 128 + t;  // reordered row
+      const bool live = hr < args.S;
+      const float inv_h = 1.f / l_h;
+      __nv_bfloat16* hrow = args.head_o + (static_cast<size_t>(it.bank) * args.S + (live ? hr : 0)) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tmem_ld32(t_ox + c * 32, v);
+        tmem_wait_ld();
+        if (!live) continue;
+        uint4* dst = reinterpret_cast<uint4*>(hrow + c * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16(v[8 * q + 0] * inv_h, v[8 * q + 1] * inv_h);
+          w.y = pack_bf16(v[8 * q + 2] * inv_h, v[8 * q + 3] * inv_h);
+          w.z = pack_bf16(v[8 * q + 4] * inv_h, v[8 * q + 5] * inv_h);
+          w.w = pack_bf16(v[8 * q + 6] * inv_h, v[8 * q + 7] * inv_h);
+          st_stream_v4(dst + q, w);
+        }
+      }
+      if (live) args.head_lse[static_cast<size_t>(it.bank) * args.S + hr] = (m_h + __log2f(l_h)) * 0.69314718055994531f;
+    };
     // Logit bound: |q.k| <= |q| |k|, so every logit of key block j is at most
     // qn_l2 * k_norm_max[j] (log2 units).  From the second block on, a warp whose rows all
     // satisfy bound <= m_run + kBoundSlack exponentiates against m_run as it stands: no row
@@ -536,6 +613,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
+      // O is complete up to block r - 1 (the commit of S(r) covers PV(r - 1)) and PV(r) waits
+      // for this warp's pfull arrival: the kept blocks' output can be read now.
+      if (refresh && r == head_round) write_head(m_run, l_run);
       float s[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(t_sx + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
@@ -646,6 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok) {
       tc_fence_after();
+      if (refresh && head_round >= Lx) write_head(m_run, l_run);  // the tile keeps every block
       const bool in_seq = pos >= 0 && pos < args.S;  // a corrupt index writes nothing
       if (!in_seq) pos = 0;
       const float inv_l = 1.f / l_run;
@@ -763,14 +844,24 @@ int launch_fmha(const FmhaLaunch& L, cudaStream_t stream) {
   if (grid <= 0) return kOk;
   if (L.D == 128) {
     const int smem = FmhaSmem<128>::kTotal + 1024;
-    cudaFuncSetAttribute(fmha_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    fmha_fwd_kernel<128><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.tm_go, L.tm_det, a);
+    if (a.refresh) {
+      cudaFuncSetAttribute(fmha_fwd_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      fmha_fwd_kernel<128, true><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.tm_go, L.tm_det, a);
+    } else {
+      cudaFuncSetAttribute(fmha_fwd_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      fmha_fwd_kernel<128, false><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.tm_go, L.tm_det, a);
+    }
   } else if (L.D == 64) {
     // request enough shared memory for one CTA per SM (TMEM holds one CTA's 512 columns)
     int smem = FmhaSmem<64>::kTotal + 1024;
     if (smem < 120 * 1024) smem = 120 * 1024;
-    cudaFuncSetAttribute(fmha_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    fmha_fwd_kernel<64><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.tm_go, L.tm_det, a);
+    if (a.refresh) {
+      cudaFuncSetAttribute(fmha_fwd_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      fmha_fwd_kernel<64, true><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.tm_go, L.tm_det, a);
+    } else {
+      cudaFuncSetAttribute(fmha_fwd_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      fmha_fwd_kernel<64, false><<<grid, kThreads, smem, stream>>>(L.tm_q, L.tm_k, L.tm_vt, L.tm_go, L.tm_det, a);
+    }
   } else {
     return kErrShape;
   }

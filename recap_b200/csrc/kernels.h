@@ -141,6 +141,11 @@ int launch_center(const CenterArgs& a, cudaStream_t s);
 struct FmhaArgs {
   int banks, S, S_pad, NB, nB, dense_start, rows;
   int all_blocks;          // 1: every key block (dense attention)
+  // 1 (with all_blocks): every key block, the partition's kept blocks first; each row's
+  // output and LSE over the kept blocks alone go to head_o / head_lse on the way
+  int refresh;
+  __nv_bfloat16* head_o;   // [banks, S, D] reordered (refresh)
+  float* head_lse;         // [banks, S] reordered (refresh)
   float scale_log2;        // softmax scale * log2(e)
   const uint8_t* partition;  // [banks, nB, nB]
   const float* k_norm_max;   // [banks, NB] largest |k| per key block (nullable: always exact maxima)

@@ -74,9 +74,16 @@ __global__ void __launch_bounds__(256) select_kernel(const SelectArgs a) {
     for (int b = lane; b < 256; b += 32) h[b] = 0;
     __syncwarp();
     const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
-    for (int j = lane; j < nB; j += 32) {
-      const uint32_t key = k[j];
-      if ((key & hi_mask) == prefix) atomicAdd(&h[(key >> shift) & 0xFFu], 1u);
+    // Scores of one row lie close together, so most keys of a pass share a digit: the lanes
+    // with equal digits add their count once (one shared-memory atomic per distinct digit
+    // of the warp instead of up to 32 serialised ones on the same bin).
+    for (int base = 0; base < nB; base += 32) {
+      const int j = base + lane;
+      const uint32_t key = j < nB ? k[j] : 0u;
+      const bool hit = j < nB && (key & hi_mask) == prefix;
+      const uint32_t bin = (key >> shift) & 0xFFu;
+      const unsigned peers = __match_any_sync(0xffffffffu, hit ? bin : 0x100u);
+      if (hit && lane == __ffs(peers) - 1) atomicAdd(&h[bin], static_cast<uint32_t>(__popc(peers)));
     }
     __syncwarp();
     // lane l owns bins 255-8l .. 248-8l (descending)

@@ -8,9 +8,9 @@ controller and the model processors run on it unchanged.  Every tensor operation
 call runs in ``librecap_b200.so``:
 
 ``EXACT``    one layout pass + the attention kernel over every key block.
-``REFRESH``  dense attention with LSE, block selection (first refresh or re-rank), the
-             block-sparse head, the coarse tail and the refinement write (scoring the old
-             refinement first when one exists).
+``REFRESH``  block selection, then one attention pass that gives the dense output with LSE
+             and the block-sparse head on the way, the coarse tail and the refinement write
+             (scoring the old refinement first when one exists).
 ``SPARSE``   one layout pass, the closure statistics, the coarse tail (with the drift
              centre) and the block-sparse attention whose epilogue merges head, coarse tail
              and drift-weighted refinement and writes native order.
@@ -275,6 +275,24 @@ class Operator:
         )
         return out, lse
 
+    def _dense_and_head(self, inputs: LayerInputs, partition: torch.Tensor, scale: float, status):
+        """One pass over every key block: the dense output and LSE in native order, and the
+        block-sparse head output and LSE (kept blocks only) in reordered order."""
+        sh = inputs.shapes
+        dev = inputs.q.device
+        out = torch.empty(sh.batch, sh.heads, sh.S, sh.D, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(sh.banks, sh.S, dtype=torch.float32, device=dev)
+        head_o = torch.empty(sh.banks, sh.S, sh.D, dtype=torch.bfloat16, device=dev)
+        head_lse = torch.empty(sh.banks, sh.S, dtype=torch.float32, device=dev)
+        self.launches.run(
+            "recap_refresh_attention", 1,
+            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(partition),
+            _lib.ptr(inputs.k_norm_max), sh.banks, sh.S, sh.D, sh.n_video, float(scale),
+            _lib.ptr(gather_rows(self.layout, dev)), _lib.ptr(out), _lib.ptr(lse), _lib.ptr(head_o),
+            _lib.ptr(head_lse), _lib.ptr(status), _lib.stream_handle(dev),
+        )
+        return out, lse, head_o, head_lse
+
     def _head(self, inputs: LayerInputs, partition: torch.Tensor, scale: float, status):
         """Block-sparse head: output and LSE in reordered order."""
         sh = inputs.shapes
@@ -310,7 +328,15 @@ class Operator:
     @torch.no_grad()
     def _refresh(self, layer: SparseAttention, bank: DetailBank, query, key, value) -> torch.Tensor:
         """Dense output; stores the refinement and measures the previous one
-        (recap/operator.py:331-473)."""
+        (recap/operator.py:331-473).
+
+        The re-selection test of a revalidating refresh (recap/operator.py:420-435) depends
+        only on the block means of Q and K, so it runs first: the new selection and its
+        layer-wide overlap with the old partition decide, before any attention, which
+        partition the new refinement is stored under.  The old partition's head and coarse
+        tail score the old refinement and, when the partition is kept, also give the new
+        one, so one pass over every key block yields the dense output and that head.  Only
+        a re-selection needs a second head pass, under the new partition."""
         scale = self._scale(query)
         dev = query.device
         status = self.status_word(dev)
@@ -321,10 +347,15 @@ class Operator:
             # reference fails on the mismatch): start over as a first refresh.
             bank.release()
         revalidating = bank.valid
-        if not revalidating:
-            bank.set_partition(layer.head_partition(inputs, scale), sh.S, sh.n_video)
-        full_out, full_lse = self._dense(inputs, scale, status)
-        head_o, head_lse = self._head(inputs, bank.partition, scale, status)
+        selection = layer.head_partition(inputs, scale)
+        reselect = False
+        if revalidating:
+            # keep the old partition if the selection barely changed over the whole layer
+            kept, total = self._layer_overlap(selection, bank.partition)
+            reselect = not keep_partition(kept, total, self.config.rerank_min_overlap)
+        else:
+            bank.set_partition(selection, sh.S, sh.n_video)
+        full_out, full_lse, head_o, head_lse = self._dense_and_head(inputs, bank.partition, scale, status)
         context = layer.coarse_tail_context(inputs, scale)
         old_lse = bank.coarse_lse if revalidating else None
         coarse, coarse_lse, center = layer.coarse_tail_apply(
@@ -339,20 +370,8 @@ class Operator:
         if stats is not None:
             bank.pending_stats = stats
             bank.pending_age = self.step - bank.refreshed_at
-
-        if revalidating:
-            # Re-select the key blocks from the current attention; keep the old partition if
-            # the selection barely changed over the whole layer.
-            partition = layer.head_partition(inputs, scale)
-            if bank.partition is not None:
-                kept, total = self._layer_overlap(partition, bank.partition)
-                if keep_partition(kept, total, self.config.rerank_min_overlap):
-                    bank.coarse_lse = coarse_lse.clone()
-                    bank.refreshed_at = self.step
-                    bank.valid = True
-                    self.refreshed_layers += 1
-                    return full_out
-            bank.set_partition(partition, sh.S, sh.n_video)
+        if reselect:
+            bank.set_partition(selection, sh.S, sh.n_video)
             del head_o, head_lse, coarse, coarse_lse
             head_o, head_lse = self._head(inputs, bank.partition, scale, status)
             coarse, coarse_lse, _ = layer.coarse_tail_apply(inputs, context, bank.partition, scale, status=status)

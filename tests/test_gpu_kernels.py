@@ -221,6 +221,67 @@ def test_fmha_uneven_pairs_vs_oracle(d):
     assert lerr <= 2e-3, f"LSE max abs err {lerr}"
 
 
+def _refresh_attention(q_r, k_r, v_t, part, banks, S, d, nv, knm):
+    from recap_b200 import _lib as lib
+
+    out = torch.empty(banks, S, d, dtype=torch.bfloat16, device=DEV)
+    lse = torch.empty(banks, S, dtype=torch.float32, device=DEV)
+    head = torch.empty(banks, S, d, dtype=torch.bfloat16, device=DEV)
+    head_lse = torch.empty(banks, S, dtype=torch.float32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    lib.call("recap_refresh_attention", lib.ptr(q_r), lib.ptr(k_r), lib.ptr(v_t), lib.ptr(part), lib.ptr(knm),
+             banks, S, d, nv, 1 / math.sqrt(d), None, lib.ptr(out), lib.ptr(lse), lib.ptr(head),
+             lib.ptr(head_lse), lib.ptr(status), lib.stream_handle(torch.device(DEV)))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, f"device status {int(status.item())}"
+    return out, lse, head, head_lse
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("nv,text,text_first,dens", [(2048, 0, False, "flat"), (700, 50, True, "flat"),
+                                                     (504, 40, False, "flat"), (128 * 22 + 50, 60, False, "uneven"),
+                                                     (128 * 21, 0, False, "uneven")])
+def test_refresh_attention_head_and_dense(d, nv, text, text_first, dens):
+    """The fused REFRESH pass: its head output and LSE equal the block-sparse pass's bit for
+    bit (same kept blocks in the same order, same arithmetic), and its dense output and LSE
+    match exact fp32 attention within the parity tolerance (max-abs 2e-2 on O, 2e-3 on LSE).
+    Uneven densities (rows keeping one block next to rows keeping all) give pairs whose kept
+    lists differ in length, so the middle rounds load separate tiles while the first and
+    last rounds share them; an odd block count leaves one CTA with a single query block."""
+    lay = _layout(nv, text, text_first)
+    q, k, v = _strided_qkv(1, 2, nv + text, d, seed=21)
+    _, inp = _run_gather(lay, q, k, v, q_mean=False)
+    sh = inp.shapes
+    g = torch.Generator().manual_seed(22)
+    if dens == "flat":
+        part = torch.rand(sh.banks, sh.nB, sh.nB, generator=g) < 0.3
+    else:
+        rate = torch.rand(sh.banks, sh.nB, 1, generator=g)
+        rate[:, ::5] = 0.0
+        rate[:, 3::7] = 1.0
+        part = torch.rand(sh.banks, sh.nB, sh.nB, generator=g) < rate
+    if nv % 128:
+        part[:, -1, :] = True
+        part[:, :, -1] = True
+    part = part.to(DEV)
+    out, lse, head, head_lse = _refresh_attention(inp.q, inp.k, inp.v_t, part, sh.banks, sh.S, d, nv,
+                                                  inp.k_norm_max)
+    ref_head, ref_head_lse = _fmha(inp.q, inp.k, inp.v_t, part, sh.banks, sh.S, d, nv, False, knm=inp.k_norm_max)
+    assert torch.equal(head, ref_head)
+    assert torch.equal(head_lse, ref_head_lse)
+    qr = inp.q[:, : sh.S].float()
+    kr = inp.k[:, : sh.S].float()
+    vr = inp.v_t[:, :, : sh.S].transpose(1, 2).float()
+    s = torch.bmm(qr, kr.transpose(1, 2)) / math.sqrt(d)
+    ref_lse = torch.logsumexp(s, -1)
+    ref = torch.bmm(torch.softmax(s, -1), vr)
+    err = (out.float() - ref).abs().max().item()
+    lerr = (lse - ref_lse).abs().max().item()
+    print(f"dense O max abs {err:.3e}, LSE max abs {lerr:.3e}")
+    assert err <= 2e-2, f"O max abs err {err}"
+    assert lerr <= 2e-3, f"LSE max abs err {lerr}"
+
+
 def test_layout_key_norm_bounds():
     """The layout pass's norm bounds: the largest |k| over each 128-token block (text
     included) and |bf16(kbar)| of each video block."""
