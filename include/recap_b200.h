@@ -176,8 +176,10 @@ int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, co
  * block_sparse_exact head of recap/operator.py:366-373 (recap/kernels/block_sparse.py:78-139).
  * Each query block walks its kept key blocks first, in the order the block-sparse pass
  * takes them, writes the head output and LSE, then walks the omitted blocks to the dense
- * result.  The head equals recap_block_sparse_fmha's (all_blocks = 0, out_pos NULL, the same
- * k_norm_max) bit for bit: the same kept blocks in the same order and the same arithmetic.
+ * result.  On the query blocks below dense_start (every row a refinement reads) the head
+ * equals recap_block_sparse_fmha's (all_blocks = 0, out_pos NULL, the same k_norm_max) bit
+ * for bit: the same kept blocks in the same order and the same arithmetic.  The dense query
+ * blocks attend every key block in both, in an order that can differ (fp32 rounding).
  *   out / lse           [banks, S, D] bf16 / [banks, S] fp32 dense result, reordered row r at
  *                       row out_pos[r] (out_pos NULL: row r)
  *   head_out / head_lse [banks, S, D] bf16 / [banks, S] fp32 head result, reordered order */

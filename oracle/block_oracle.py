@@ -270,7 +270,7 @@ class BlockOracle:
             kmask = self._kernel_mask(partition)
             lse_all = torch.empty(banks, self.rows)
             margin = torch.empty(banks, self.rows, dtype=torch.float64)
-            values, masses = {}, {}
+            values, masses, dens = {}, {}, {}
             err = torch.zeros(2, dtype=torch.float64)
             center = None
             per_bank = []
@@ -284,7 +284,7 @@ class BlockOracle:
                 center = orc.drift_center(lse_all, validate_with)
             for qb in video:
                 r0, r1 = qb * BLOCK, (qb + 1) * BLOCK
-                det_b, dl_b = [], []
+                det_b, dl_b, den_b = [], [], []
                 for b in range(banks):
                     oh, lh = self._head_rows(q_r, k_r, v_r, kmask, b, qb, scale)
                     of, lf = dense[qb][b]
@@ -299,8 +299,12 @@ class BlockOracle:
                         err += stats
                     det_b.append(det[0])
                     dl_b.append(dl[0])
+                    # the tail's share of the dense mass, 1 - ratio (the refinement's weight)
+                    den_b.append(1.0 - torch.clamp(torch.exp(torch.clamp(lh - lf, max=0.0)), max=1.0 - 1e-6))
                 values[qb] = torch.stack(det_b)
                 masses[qb] = torch.stack(dl_b)
+                dens[qb] = torch.stack(den_b).float()
+            self.trace["den"] = dens
             return lse_all, values, masses, (err if validate_with is not None else None), center
 
         old_lse = st.coarse_lse if revalidating else None

@@ -36,8 +36,9 @@
 // block-sparse head over the same Q, K, V): every key block, with each tile's kept
 // blocks first, in the order the sparse step walks them.  When a tile's softmax reaches
 // its first omitted block, O holds exactly the kept blocks' products, so that tile's
-// head output and LSE are written then (the same arithmetic and order as the head-only
-// pass, so the same bits); the walk goes on over the omitted blocks to the dense result.
+// head output and LSE are written then (for the query blocks below dense_start the same
+// arithmetic and order as the head-only pass, so the same bits); the walk goes on over
+// the omitted blocks to the dense result.
 // Lists: A = [both keep | A only | B only | neither], B = [both | B only | A only |
 // neither], so the first and last parts share their K / V^T tiles.
 #include "common.cuh"

@@ -211,12 +211,20 @@ def test_operator_full_length_parity(name):
     exp = oracle.refresh(*x[0], basis=basis, partition=part0)
     _check_rows("r0", gpu["r0"], exp, oracle, stats, ulps=1)
     flip0 = _flips("r0", oracle, lse0)
+    # The refinement value det = (of - ratio oh) / (1 - ratio) - go carries the bf16 roundings
+    # of the dense and head outputs divided by the tail's share 1 - ratio (down to 1e-3), so
+    # it is compared weighted by that share: the sparse step adds det to the tail, whose
+    # weight in the merge is proportional to it (recap/kernels/detail_cache.py:267-292).
+    worst = 0.0
     for qb in oracle.state.value:
         r0, r1 = qb * 128, (qb + 1) * 128
         ok = ~flip0[:, r0:r1]
-        dv = bo.compare_bf16(value0[:, r0:r1][ok].float(), oracle.state.value[qb][ok].float())
-        assert dv["mean_rel"] <= 5e-2, (qb, dv)
+        w = oracle.trace["den"][qb][ok][:, None]
+        dv = bo.compare_bf16(value0[:, r0:r1][ok].float() * w, oracle.state.value[qb][ok].float() * w)
+        worst = max(worst, dv["mean_rel"])
+        assert dv["mean_rel"] <= 2e-2, (qb, dv)
         assert float((mass0[:, r0:r1] - oracle.state.log_mass[qb])[ok].abs().max()) <= 5e-2
+    print(f"r0 refinement value (weighted by the tail share): worst block mean_rel {worst:.3e}")
 
     oracle.step = 1
     exp = oracle.sparse(*x[1])
