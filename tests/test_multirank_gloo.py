@@ -91,3 +91,59 @@ def test_rank_leaving_makes_peer_collective_fail_not_hang():
     assert not alive, "a rank hung on a collective"
     assert results.get(1) == "left"
     assert str(results.get(0, "")).startswith("error"), results.get(0)
+
+
+def _global_qkv(S: int, H: int, d: int) -> torch.Tensor:
+    """[S, 3, H, d] with every element naming its (token, tensor, head, column)."""
+    t = torch.arange(S).view(S, 1, 1, 1) * 1000.0
+    i = torch.arange(3).view(1, 3, 1, 1) * 100.0
+    h = torch.arange(H).view(1, 1, H, 1) * 10.0
+    c = torch.arange(d).view(1, 1, 1, d) * 1.0
+    return t + i + h + c
+
+
+def _ulysses_worker(rank: int, world: int, port: int, results):
+    from recap_b200.ulysses import check_split, heads_to_seq, seq_to_heads
+
+    _init(rank, world, port)
+    try:
+        S, H, d = 12, 4, 3
+        s, h = check_split(S, H, world)
+        full = _global_qkv(S, H, d)
+        mine = full[rank * s:(rank + 1) * s].contiguous()  # this rank's tokens, every head
+        q, k, v = seq_to_heads(mine, world, dist.group.WORLD)
+        # every token of this rank's heads, as the operator's [1, h, S, d]
+        ok = all(torch.equal(x[0], full[:, i, rank * h:(rank + 1) * h].permute(1, 0, 2))
+                 for i, x in enumerate((q, k, v)))
+        # stand-in attention output: distinct per (head, token, column)
+        out = (q * 2.0 + 1.0).contiguous()
+        back = heads_to_seq(out, world, dist.group.WORLD)  # [s, H d]
+        expect = (full[rank * s:(rank + 1) * s, 0] * 2.0 + 1.0).reshape(s, H * d)
+        results[rank] = (ok, bool(torch.equal(back, expect)), tuple(q.shape), tuple(back.shape))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ulysses_layout_switch_round_trip():
+    """The sequence -> head switch hands each rank every token of its heads in token order,
+    and the head -> sequence switch returns each rank its own tokens of every head in the
+    global head order (world size 2, gloo all_to_all_single on CPU)."""
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    port = _port()
+    mp.start_processes(_ulysses_worker, args=(2, port, results), nprocs=2, start_method="spawn", join=True)
+    for r in range(2):
+        assert results[r] == (True, True, (1, 2, 12, 3), (6, 12)), results[r]
+
+
+def test_ulysses_single_rank_is_identity_and_rejects_uneven_splits():
+    from recap_b200.ulysses import check_split, heads_to_seq, seq_to_heads
+
+    full = _global_qkv(10, 4, 3)
+    q, k, v = seq_to_heads(full, 1)
+    assert torch.equal(q[0], full[:, 0].permute(1, 0, 2))
+    assert torch.equal(heads_to_seq(v.contiguous(), 1), full[:, 2].reshape(10, 12))
+    with pytest.raises(ValueError):
+        check_split(10, 4, 4)
+    with pytest.raises(ValueError):
+        check_split(12, 6, 4)
