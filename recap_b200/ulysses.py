@@ -50,9 +50,11 @@ def seq_to_heads(qkv: torch.Tensor, world: int, group=None) -> tuple[torch.Tenso
     if three != 3 or H % world:
         raise ValueError("qkv must be [tokens, 3, heads, dim] with heads divisible by the world size")
     h = H // world
-    send = qkv.view(s, 3, world, h, d).permute(2, 0, 1, 3, 4).contiguous()
-    recv = _exchange(send, group) if world > 1 else send
-    full = recv.view(world * s, 3, h, d)
+    if world == 1:
+        full = qkv  # nothing to exchange: the heads are views of the projection output
+    else:
+        send = qkv.view(s, 3, world, h, d).permute(2, 0, 1, 3, 4).contiguous()
+        full = _exchange(send, group).view(world * s, 3, h, d)
     q, k, v = (full[:, i].permute(1, 0, 2).unsqueeze(0) for i in range(3))
     return q, k, v
 
@@ -67,6 +69,8 @@ def heads_to_seq(out: torch.Tensor, world: int, group=None) -> torch.Tensor:
     if S % world:
         raise ValueError("the sequence must split evenly over the world size")
     s = S // world
+    if world == 1:
+        return out[0].permute(1, 0, 2).reshape(S, h * d)
     send = out[0].reshape(h, world, s, d).permute(1, 2, 0, 3).contiguous()  # [P, s, h, d]
-    recv = _exchange(send, group) if world > 1 else send  # [P (head group), s, h, d]
+    recv = _exchange(send, group)  # [P (head group), s, h, d]
     return recv.permute(1, 0, 2, 3).reshape(s, world * h * d)
