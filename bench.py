@@ -72,6 +72,9 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default=WORKLOAD["name"],
                    help="BASELINE config 4 (default), 2 or 3")
+    p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                   help="stack workload: the Ulysses exchange fused into the layout pass and the attention "
+                        "epilogue over NVLink peer memory (p2p), or NCCL all_to_all_single around the call")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true", help="skip the CPU oracle check of the last timed output")
@@ -643,10 +646,11 @@ class AttentionStack:
     PHASES = ("qkv_projection", "all_to_all_seq_to_heads", "attention", "all_to_all_heads_to_seq",
               "out_projection")
 
-    def __init__(self, op, w: dict, world: int, group, device):
-        from recap_b200.ulysses import check_split
+    def __init__(self, op, w: dict, world: int, group, device, exchange: str = "nccl"):
+        from recap_b200.ulysses import PeerBuffer, ShardedIO, check_split
 
         self.op, self.world, self.group = op, world, group
+        self.exchange = exchange if world > 1 else "nccl"
         self.heads, self.dim, self.hidden = w["heads"], w["dim"], w["hidden"]
         self.S = w["grid"][0] * w["grid"][1] * w["grid"][2] + w["text"]
         self.s, self.h = check_split(self.S, self.heads, world)
@@ -661,6 +665,27 @@ class AttentionStack:
                     for _ in range(w["layers"])]
         self.timing = False
         self.events: list[list] = []
+        self.io = None
+        if self.exchange == "p2p":
+            # the projection output and the attention output of every rank, reachable by all
+            self.peer_qkv = PeerBuffer(self.s * 3 * hd * 2, group, device)
+            self.peer_out = PeerBuffer(self.s * hd * 2, group, device)
+            self.io = ShardedIO(self.peer_qkv, self.peer_out, self.heads, self.dim, self.S)
+            self.flag = torch.zeros(1, device=device)
+
+    def close(self) -> None:
+        if self.io is not None:
+            self.peer_qkv.close()
+            self.peer_out.close()
+            self.io = None
+
+    def _meet(self) -> None:
+        """Every rank's writes so far are done before any rank goes on (a one-element
+        all-reduce on the stream: its kernel starts after this rank's earlier work and ends
+        after every rank's)."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self.flag, group=self.group)
 
     def _mark(self, marks: list) -> None:
         if self.timing:
@@ -672,6 +697,8 @@ class AttentionStack:
         """One denoising step's attention layers on this rank's tokens ``[s, hidden]``."""
         from recap_b200.ulysses import heads_to_seq, seq_to_heads
 
+        if self.io is not None:
+            return self._step_p2p(x)
         for layer in range(len(self.w_qkv)):
             marks: list = []
             self._mark(marks)
@@ -682,6 +709,31 @@ class AttentionStack:
             o = self.op.attend(layer, q, k, v)
             self._mark(marks)
             y = heads_to_seq(o, self.world, self.group)
+            self._mark(marks)
+            x = x + y @ self.w_o[layer]
+            self._mark(marks)
+            if self.timing:
+                self.events.append(marks)
+        return x
+
+    def _step_p2p(self, x: torch.Tensor) -> torch.Tensor:
+        """The layer with the exchange in place: the projection writes this rank's shard of
+        the shared buffer, the layout pass reads every rank's shard of this rank's heads
+        over NVLink, and the attention epilogue stores each output row into the shard of
+        the rank that owns the token."""
+        io = self.io
+        qkv = io.local_qkv().view(self.s, 3 * self.heads * self.dim)
+        y = io.local_out()
+        for layer in range(len(self.w_qkv)):
+            marks: list = []
+            self._mark(marks)
+            torch.matmul(x, self.w_qkv[layer], out=qkv)
+            self._mark(marks)
+            self._meet()  # every shard written before any rank reads
+            self._mark(marks)
+            self.op.attend_sharded(layer, io)
+            self._mark(marks)
+            self._meet()  # every output row stored, every shard read
             self._mark(marks)
             x = x + y @ self.w_o[layer]
             self._mark(marks)
@@ -714,7 +766,7 @@ def run_stack(args, w: dict, world: int, rank: int, dev, group) -> None:
                                      text_first=w["text_first"])
     op = Operator.build(OperatorConfig(head_density=w["density"]), SparseGeometry.build(layout, 128),
                         n_layers=w["layers"], process_group=group)
-    stack = AttentionStack(op, w, world, group, dev)
+    stack = AttentionStack(op, w, world, group, dev, exchange=args.exchange)
     mine = range(rank * stack.s, (rank + 1) * stack.s)
     xs = [stack_hidden(w, mine, w["hidden"], seed=s, device=dev) for s in (0, 1, 2)]
 
@@ -756,6 +808,7 @@ def run_stack(args, w: dict, world: int, rank: int, dev, group) -> None:
         timed(SPARSE, 1, step, phases=True)
         phases = stack.take_phases()
         op.check_device_status()
+        stack.close()
     total = sum(phases.values())
     a2a = phases["all_to_all_seq_to_heads"] + phases["all_to_all_heads_to_seq"]
     n_refresh = -(-w["schedule_steps"] // w["refresh_every"])
@@ -769,7 +822,8 @@ def run_stack(args, w: dict, world: int, rank: int, dev, group) -> None:
             "data": "synthetic: seeded smooth low-rank (rank 16) + 0.5 noise hidden states, random-init projections",
             "config": {"workload": w["name"], "layers": w["layers"], "hidden": w["hidden"], "heads": w["heads"],
                        "head_dim": w["dim"], "seq_len": stack.S, "keep": max(1, round(w["density"] * -(-(stack.S - w["text"]) // 128))),
-                       "parallelism": f"ulysses sequence/{world} + heads/{world}", "bank": "HBM",
+                       "parallelism": f"ulysses sequence/{world} + heads/{world}", "exchange": stack.exchange,
+                       "bank": "HBM",
                        "l2": "per-layer inputs > 126 MB L2 (no flush needed)"},
             "us_per_layer": round(sparse_ms * 1000.0 / w["layers"], 1),
             "refresh_step_ms": round(refresh_ms, 2),
@@ -778,6 +832,9 @@ def run_stack(args, w: dict, world: int, rank: int, dev, group) -> None:
                         f"{n_refresh} x REFRESH + {w['schedule_steps'] - n_refresh} x SPARSE, from the measured steps",
             "phases_ms_per_step": {k: round(v, 3) for k, v in phases.items()},
             "all_to_all_share": round(a2a / total, 4) if total else None,
+            "exchange_phases": ("NCCL all_to_all_single with the layout copies around it" if stack.exchange == "nccl"
+                                else "the two one-element all-reduces that order the ranks' buffer writes; the "
+                                     "transfers themselves run inside the layout pass and the attention epilogue"),
             "gpu_launches": gpu_launches,
             "clocks": clk.summary(),
         }

@@ -13,7 +13,8 @@
  *  - "Reordered" means the token order [Hilbert-ordered video | text] of
  *    recap/sparse/layout.py; "native" is the model's own order.
  *  - Every entry point returns 0 on success or a RECAP_ERR_* code.  Nothing
- *    synchronises the stream or allocates device memory; scratch buffers come
+ *    synchronises the stream or allocates device memory (except recap_peer_alloc,
+ *    the allocator of buffers shared between ranks); scratch buffers come
  *    from the caller.  Kernels that wait on on-chip barriers give up after a
  *    bounded time and record RECAP_STATUS_* in the caller's `status` word
  *    (device int, zero-initialised), which the caller reads after the stream.
@@ -28,7 +29,7 @@
 extern "C" {
 #endif
 
-#define RECAP_B200_ABI_VERSION 7
+#define RECAP_B200_ABI_VERSION 8
 
 #define RECAP_OK 0
 #define RECAP_ERR_SHAPE 1
@@ -75,6 +76,22 @@ int recap_layout_gather(const void* q, const void* k, const void* v, const int64
                         float* v_mean, void* k_mean_bf16, void* v_mean_t_bf16, void* k_centred_t,
                         const float* basis, int rank, float* variance, void* variance_bf16,
                         float* k_norm_max, float* k_mean_norm, void* stream);
+
+/* recap_layout_gather for a sequence-parallel layer whose projections stay sharded by token:
+ * rank q of n_ranks holds native tokens [q tokens_per_rank, (q + 1) tokens_per_rank), and
+ * q_ranks[q] / k_ranks[q] / v_ranks[q] (host arrays of device pointers, one per rank, each
+ * 16-byte aligned; other ranks' buffers opened with recap_peer_import) point at head 0 of its
+ * first token, with the element strides of `strides` (batch 1).  The pass reads every rank's
+ * rows directly, over NVLink for the other GPUs, so the sequence-to-head all-to-all of a
+ * Ulysses layer (the exchange around Operator.attend in recap's multi-GPU runs) is this
+ * gather's load.  n_ranks in [2, 8] with n_ranks * tokens_per_rank = S.  The caller orders
+ * the ranks' writes of their shards before this launch (a collective on the stream). */
+int recap_layout_gather_ranks(const void* const* q_ranks, const void* const* k_ranks, const void* const* v_ranks,
+                              int n_ranks, int tokens_per_rank, const int64_t* strides, int heads, int S, int D,
+                              int n_video, const int32_t* src_row, void* q_reordered, void* k_reordered,
+                              void* v_transposed, float* q_mean, float* k_mean, float* v_mean, void* k_mean_bf16,
+                              void* v_mean_t_bf16, void* k_centred_t, const float* basis, int rank, float* variance,
+                              void* variance_bf16, float* k_norm_max, float* k_mean_norm, void* stream);
 
 /* Largest closure rank the layout pass folds itself (larger ranks: recap_closure_stats). */
 int recap_gather_max_rank(void);
@@ -188,6 +205,19 @@ int recap_refresh_attention(const void* q_reordered, const void* k_reordered, co
                             int n_video, float scale, const int32_t* out_pos, void* out, float* lse,
                             void* head_out, float* head_lse, int* status, void* stream);
 
+/* recap_refresh_attention with the dense output written into the token shards of the ranks
+ * of a sequence-parallel layer: bank b, native token n goes to out_ranks[q] + b out_bank_stride
+ * + (n - q tokens_per_rank) out_row_stride (elements) with q = n / tokens_per_rank, straight
+ * over NVLink for other GPUs (the head-to-sequence all-to-all after Operator.attend).
+ * n_ranks in [2, 8], n_ranks * tokens_per_rank = S, strides multiples of 8, row stride >= D;
+ * each out_ranks[q] 16-byte aligned.  The kernel ends with a system-scope fence; the caller
+ * orders the ranks' reads of their shards after it (a collective on the stream). */
+int recap_refresh_attention_ranks(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                                  const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
+                                  int n_video, float scale, const int32_t* out_pos, void* const* out_ranks,
+                                  int n_ranks, int tokens_per_rank, int64_t out_bank_stride, int64_t out_row_stride,
+                                  float* lse, void* head_out, float* head_lse, int* status, void* stream);
+
 /* The corrected SPARSE step: block-sparse attention with the drift-weighted merge of the coarse
  * tail and the cached refinement fused as its epilogue, written in native order.
  * Replaces block_sparse_exact + sparse_merge (recap/kernels/detail_cache.py:402-456) +
@@ -200,6 +230,15 @@ int recap_sparse_step(const void* q_reordered, const void* k_reordered, const vo
                       const void* coarse_out, const float* coarse_lse, const void* detail_value,
                       const float* detail_log_mass, const float* old_lse, const float* center,
                       const int32_t* out_pos, void* out, int* status, void* stream);
+
+/* recap_sparse_step with the output written into the token shards of the ranks of a
+ * sequence-parallel layer, as recap_refresh_attention_ranks places it. */
+int recap_sparse_step_ranks(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                            const uint8_t* partition, const float* k_norm_max, int banks, int S, int D, int n_video,
+                            float scale, const void* coarse_out, const float* coarse_lse, const void* detail_value,
+                            const float* detail_log_mass, const float* old_lse, const float* center,
+                            const int32_t* out_pos, void* const* out_ranks, int n_ranks, int tokens_per_rank,
+                            int64_t out_bank_stride, int64_t out_row_stride, int* status, void* stream);
 
 /* Number of (err^2, ref^2) float pairs of scratch `partials` recap_refresh_detail needs. */
 int recap_refresh_partials(int banks, int n_video);
@@ -250,6 +289,26 @@ int recap_exp2_check(const float* in, float* out, int n, void* stream);
  * the first / second wait completed (expected 0); result[2]: the second waiter's time
  * in ns (about limit_ns, not 4x).  Nothing faults or hangs; the context stays usable. */
 int recap_wait_selftest(int* status, long long limit_ns, long long* result, void* stream);
+
+/* Buffers shared between the ranks of a sequence-parallel layer (one process per GPU), by CUDA
+ * IPC: recap_peer_alloc allocates `bytes` on the current device (cudaMalloc), recap_peer_export
+ * writes its recap_peer_handle_bytes()-byte handle, another process opens it with
+ * recap_peer_import (peer access enabled on first use) and releases it with recap_peer_close;
+ * the owner frees it with recap_peer_free after every importer has closed it.  No counterpart
+ * in the reference: they carry the token shards recap_layout_gather_ranks reads and the
+ * *_ranks attention passes write. */
+int recap_peer_alloc(int64_t bytes, void** ptr);
+int recap_peer_free(void* ptr);
+int recap_peer_handle_bytes(void);
+int recap_peer_export(void* ptr, void* handle_out);
+int recap_peer_import(const void* handle, void** ptr);
+int recap_peer_close(void* ptr);
+
+/* Copy a [banks, S, D] bf16 output into the ranks' token shards as the *_ranks attention passes
+ * place it (copy engines; peer copies over NVLink): the step after a REFRESH whose dense
+ * output the refinement write reads locally.  No counterpart in the reference. */
+int recap_scatter_rows(const void* src, int banks, int S, int D, void* const* out_ranks, int n_ranks,
+                       int tokens_per_rank, int64_t out_bank_stride, int64_t out_row_stride, void* stream);
 
 #ifdef __cplusplus
 }

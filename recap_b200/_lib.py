@@ -16,7 +16,7 @@ import torch
 PACKAGE_DIR = Path(__file__).resolve().parent
 LIB_PATH = PACKAGE_DIR / "librecap_b200.so"
 
-ABI_VERSION = 7  # RECAP_B200_ABI_VERSION of include/recap_b200.h
+ABI_VERSION = 8  # RECAP_B200_ABI_VERSION of include/recap_b200.h
 
 RECAP_OK = 0
 RECAP_ERR_SHAPE = 1
@@ -43,6 +43,8 @@ SIGNATURES: dict[str, tuple] = {
     "recap_abi_version": (_I, []),
     "recap_layout_gather": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                  _P, _I, _P, _P, _P, _P, _P]),
+    "recap_layout_gather_ranks": (_I, [_P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                       _P, _P, _I, _P, _P, _P, _P, _P]),
     "recap_gather_max_rank": (_I, []),
     "recap_cvk_workspace_floats": (_I64, [_I, _I, _I]),
     "recap_value_key_covariance": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
@@ -56,6 +58,17 @@ SIGNATURES: dict[str, tuple] = {
                                _P, _P]),
     "recap_block_sparse_fmha": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P]),
     "recap_refresh_attention": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P]),
+    "recap_refresh_attention_ranks": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _I, _I, _I64, _I64, _P,
+                                           _P, _P, _P, _P]),
+    "recap_sparse_step_ranks": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I,
+                                     _I64, _I64, _P, _P]),
+    "recap_peer_alloc": (_I, [_I64, _P]),
+    "recap_peer_free": (_I, [_P]),
+    "recap_peer_handle_bytes": (_I, []),
+    "recap_peer_export": (_I, [_P, _P]),
+    "recap_peer_import": (_I, [_P, _P]),
+    "recap_peer_close": (_I, [_P]),
+    "recap_scatter_rows": (_I, [_P, _I, _I, _I, _P, _I, _I, _I64, _I64, _P]),
     "recap_sparse_step": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "recap_refresh_partials": (_I, [_I, _I]),
     "recap_refresh_detail": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),

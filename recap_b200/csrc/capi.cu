@@ -7,6 +7,8 @@
 #include <mutex>
 
 #include "../../include/recap_b200.h"
+#include <cstring>
+
 #include "kernels.h"
 
 namespace recap {
@@ -69,12 +71,21 @@ extern "C" {
 
 int recap_abi_version(void) { return RECAP_B200_ABI_VERSION; }
 
-int recap_layout_gather(const void* q, const void* k, const void* v, const int64_t* strides, int batch,
-                        int heads, int S, int D, int n_video, const int32_t* src_row, void* q_reordered,
-                        void* k_reordered, void* v_transposed, float* q_mean, float* k_mean, float* v_mean,
-                        void* k_mean_bf16, void* v_mean_t_bf16, void* k_centred_t, const float* basis, int rank,
-                        float* variance, void* variance_bf16, float* k_norm_max, float* k_mean_norm,
-                        void* stream) {
+}  // extern "C"
+
+// Token shards of a sequence-parallel layer: rank q holds native tokens
+// [q tokens_per_rank, (q + 1) tokens_per_rank) of every tensor at ptr[t][q].
+struct RankSources {
+  int n_ranks, tokens_per_rank;
+  const void* const* ptr[3];
+};
+
+static int gather_impl(const void* q, const void* k, const void* v, const RankSources* ranks,
+                       const int64_t* strides, int batch, int heads, int S, int D, int n_video,
+                       const int32_t* src_row, void* q_reordered, void* k_reordered, void* v_transposed,
+                       float* q_mean, float* k_mean, float* v_mean, void* k_mean_bf16, void* v_mean_t_bf16,
+                       void* k_centred_t, const float* basis, int rank, float* variance, void* variance_bf16,
+                       float* k_norm_max, float* k_mean_norm, void* stream) {
   Geom g;
   if (!geom(S, n_video, &g) || !d_ok(D) || batch <= 0 || heads <= 0 || strides == nullptr ||
       src_row == nullptr)
@@ -115,7 +126,49 @@ int recap_layout_gather(const void* q, const void* k, const void* v, const int64
   a.variance = variance;
   a.variance_bf16 = static_cast<__nv_bfloat16*>(variance_bf16);
   if ((a.kct != nullptr || a.variance != nullptr) && k == nullptr) return kErrShape;
+  if (ranks != nullptr) {
+    if (ranks->n_ranks < 2 || ranks->n_ranks > kMaxRanks || ranks->tokens_per_rank <= 0 ||
+        static_cast<int64_t>(ranks->n_ranks) * ranks->tokens_per_rank != S || batch != 1)
+      return kErrShape;
+    a.n_ranks = ranks->n_ranks;
+    a.tokens_per_rank = ranks->tokens_per_rank;
+    for (int t = 0; t < 3; ++t) {
+      if (src[t] == nullptr) continue;
+      if (ranks->ptr[t] == nullptr) return kErrShape;
+      for (int r = 0; r < ranks->n_ranks; ++r) {
+        const void* p = ranks->ptr[t][r];
+        if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15)) return kErrShape;
+        a.rank_src[r][t] = static_cast<const __nv_bfloat16*>(p);
+      }
+    }
+  }
   return launch_gather(a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" {
+
+int recap_layout_gather(const void* q, const void* k, const void* v, const int64_t* strides, int batch,
+                        int heads, int S, int D, int n_video, const int32_t* src_row, void* q_reordered,
+                        void* k_reordered, void* v_transposed, float* q_mean, float* k_mean, float* v_mean,
+                        void* k_mean_bf16, void* v_mean_t_bf16, void* k_centred_t, const float* basis, int rank,
+                        float* variance, void* variance_bf16, float* k_norm_max, float* k_mean_norm,
+                        void* stream) {
+  return gather_impl(q, k, v, nullptr, strides, batch, heads, S, D, n_video, src_row, q_reordered, k_reordered,
+                     v_transposed, q_mean, k_mean, v_mean, k_mean_bf16, v_mean_t_bf16, k_centred_t, basis, rank,
+                     variance, variance_bf16, k_norm_max, k_mean_norm, stream);
+}
+
+int recap_layout_gather_ranks(const void* const* q_ranks, const void* const* k_ranks, const void* const* v_ranks,
+                              int n_ranks, int tokens_per_rank, const int64_t* strides, int heads, int S, int D,
+                              int n_video, const int32_t* src_row, void* q_reordered, void* k_reordered,
+                              void* v_transposed, float* q_mean, float* k_mean, float* v_mean, void* k_mean_bf16,
+                              void* v_mean_t_bf16, void* k_centred_t, const float* basis, int rank, float* variance,
+                              void* variance_bf16, float* k_norm_max, float* k_mean_norm, void* stream) {
+  if (q_ranks == nullptr || k_ranks == nullptr || v_ranks == nullptr) return kErrShape;
+  RankSources rs{n_ranks, tokens_per_rank, {q_ranks, k_ranks, v_ranks}};
+  return gather_impl(q_ranks[0], k_ranks[0], v_ranks[0], &rs, strides, 1, heads, S, D, n_video, src_row,
+                     q_reordered, k_reordered, v_transposed, q_mean, k_mean, v_mean, k_mean_bf16, v_mean_t_bf16,
+                     k_centred_t, basis, rank, variance, variance_bf16, k_norm_max, k_mean_norm, stream);
 }
 
 int recap_gather_max_rank(void) { return gather_max_rank(); }
@@ -274,6 +327,30 @@ static int device_sm_count() {
   return counts[dev];
 }
 
+// Output rows placed in the token shards of the ranks of a sequence-parallel layer.
+struct OutRanks {
+  void* const* ptr;
+  int n_ranks, tokens_per_rank;
+  int64_t bank_stride, row_stride;
+};
+
+static int apply_out_ranks(FmhaArgs& a, const OutRanks& o, int D) {
+  if (o.ptr == nullptr || o.n_ranks < 2 || o.n_ranks > kMaxRanks || o.tokens_per_rank <= 0 ||
+      static_cast<int64_t>(o.n_ranks) * o.tokens_per_rank != a.S || o.bank_stride % 8 || o.row_stride % 8 ||
+      o.bank_stride < 0 || o.row_stride < D)
+    return kErrShape;
+  for (int r = 0; r < o.n_ranks; ++r) {
+    if (o.ptr[r] == nullptr || (reinterpret_cast<uintptr_t>(o.ptr[r]) & 15)) return kErrShape;
+    a.o_rank[r] = static_cast<__nv_bfloat16*>(o.ptr[r]);
+  }
+  a.o = a.o_rank[0];
+  a.n_ranks = o.n_ranks;
+  a.tokens_per_rank = o.tokens_per_rank;
+  a.o_bank_stride = o.bank_stride;
+  a.o_row_stride = o.row_stride;
+  return kOk;
+}
+
 static int fmha_common(const void* q_reordered, const void* k_reordered, const void* v_transposed, int banks,
                        int S, int D, FmhaLaunch* L) {
   Geom g;
@@ -282,6 +359,8 @@ static int fmha_common(const void* q_reordered, const void* k_reordered, const v
   const int S_pad = ((S + 127) / 128) * 128;
   L->args.q = static_cast<const __nv_bfloat16*>(q_reordered);
   L->args.num_sms = device_sm_count();
+  L->args.o_bank_stride = static_cast<int64_t>(S) * D;  // [banks, S, D] unless a caller places rows
+  L->args.o_row_stride = D;
   rc |= make_tmap_bf16(&L->tm_q, q_reordered, static_cast<uint64_t>(banks) * S_pad, D, 128);
   rc |= make_tmap_bf16(&L->tm_k, k_reordered, static_cast<uint64_t>(banks) * S_pad, D, 128);
   rc |= make_tmap_bf16(&L->tm_vt, v_transposed, static_cast<uint64_t>(banks) * D, S_pad, D);
@@ -319,11 +398,13 @@ int recap_block_sparse_fmha(const void* q_reordered, const void* k_reordered, co
   return launch_fmha(L, static_cast<cudaStream_t>(stream));
 }
 
-int recap_refresh_attention(const void* q_reordered, const void* k_reordered, const void* v_transposed,
-                            const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
-                            int n_video, float scale, const int32_t* out_pos, void* out, float* lse,
-                            void* head_out, float* head_lse, int* status, void* stream) {
+static int refresh_attention_impl(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                                  const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
+                                  int n_video, float scale, const int32_t* out_pos, void* out, float* lse,
+                                  void* head_out, float* head_lse, int* status, void* stream,
+                                  const OutRanks* sink) {
   Geom g;
+  if (sink != nullptr && sink->ptr != nullptr) out = sink->ptr[0];
   if (!geom(S, n_video, &g) || !d_ok(D) || banks <= 0 || out == nullptr || lse == nullptr ||
       partition == nullptr || head_out == nullptr || head_lse == nullptr)
     return kErrShape;
@@ -351,16 +432,36 @@ int recap_refresh_attention(const void* q_reordered, const void* k_reordered, co
   a.o = static_cast<__nv_bfloat16*>(out);
   a.lse = lse;
   a.status = status;
+  if (sink != nullptr && (rc = apply_out_ranks(a, *sink, D)) != kOk) return rc;
   return launch_fmha(L, static_cast<cudaStream_t>(stream));
 }
 
-int recap_sparse_step(const void* q_reordered, const void* k_reordered, const void* v_transposed,
-                      const uint8_t* partition, const float* k_norm_max, int banks, int S, int D, int n_video,
-                      float scale,
-                      const void* coarse_out, const float* coarse_lse, const void* detail_value,
-                      const float* detail_log_mass, const float* old_lse, const float* center,
-                      const int32_t* out_pos, void* out, int* status, void* stream) {
+int recap_refresh_attention(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                            const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
+                            int n_video, float scale, const int32_t* out_pos, void* out, float* lse,
+                            void* head_out, float* head_lse, int* status, void* stream) {
+  return refresh_attention_impl(q_reordered, k_reordered, v_transposed, partition, k_norm_max, banks, S, D, n_video,
+                                scale, out_pos, out, lse, head_out, head_lse, status, stream, nullptr);
+}
+
+int recap_refresh_attention_ranks(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                                  const uint8_t* partition, const float* k_norm_max, int banks, int S, int D,
+                                  int n_video, float scale, const int32_t* out_pos, void* const* out_ranks,
+                                  int n_ranks, int tokens_per_rank, int64_t out_bank_stride, int64_t out_row_stride,
+                                  float* lse, void* head_out, float* head_lse, int* status, void* stream) {
+  const OutRanks sink{out_ranks, n_ranks, tokens_per_rank, out_bank_stride, out_row_stride};
+  if (out_ranks == nullptr) return kErrShape;
+  return refresh_attention_impl(q_reordered, k_reordered, v_transposed, partition, k_norm_max, banks, S, D, n_video,
+                                scale, out_pos, nullptr, lse, head_out, head_lse, status, stream, &sink);
+}
+
+static int sparse_step_impl(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                            const uint8_t* partition, const float* k_norm_max, int banks, int S, int D, int n_video,
+                            float scale, const void* coarse_out, const float* coarse_lse, const void* detail_value,
+                            const float* detail_log_mass, const float* old_lse, const float* center,
+                            const int32_t* out_pos, void* out, int* status, void* stream, const OutRanks* sink) {
   Geom g;
+  if (sink != nullptr && sink->ptr != nullptr) out = sink->ptr[0];
   if (!geom(S, n_video, &g) || !d_ok(D) || banks <= 0 || out == nullptr || partition == nullptr) return kErrShape;
   if (g.rows > 0 && (coarse_out == nullptr || coarse_lse == nullptr || detail_value == nullptr ||
                      detail_log_mass == nullptr || old_lse == nullptr || center == nullptr))
@@ -402,7 +503,32 @@ int recap_sparse_step(const void* q_reordered, const void* k_reordered, const vo
     if (rc != kOk) return rc;
     a.tma_epilogue = 1;
   }
+  if (sink != nullptr && (rc = apply_out_ranks(a, *sink, D)) != kOk) return rc;
   return launch_fmha(L, static_cast<cudaStream_t>(stream));
+}
+
+int recap_sparse_step(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                      const uint8_t* partition, const float* k_norm_max, int banks, int S, int D, int n_video,
+                      float scale,
+                      const void* coarse_out, const float* coarse_lse, const void* detail_value,
+                      const float* detail_log_mass, const float* old_lse, const float* center,
+                      const int32_t* out_pos, void* out, int* status, void* stream) {
+  return sparse_step_impl(q_reordered, k_reordered, v_transposed, partition, k_norm_max, banks, S, D, n_video, scale,
+                          coarse_out, coarse_lse, detail_value, detail_log_mass, old_lse, center, out_pos, out,
+                          status, stream, nullptr);
+}
+
+int recap_sparse_step_ranks(const void* q_reordered, const void* k_reordered, const void* v_transposed,
+                            const uint8_t* partition, const float* k_norm_max, int banks, int S, int D, int n_video,
+                            float scale, const void* coarse_out, const float* coarse_lse, const void* detail_value,
+                            const float* detail_log_mass, const float* old_lse, const float* center,
+                            const int32_t* out_pos, void* const* out_ranks, int n_ranks, int tokens_per_rank,
+                            int64_t out_bank_stride, int64_t out_row_stride, int* status, void* stream) {
+  const OutRanks sink{out_ranks, n_ranks, tokens_per_rank, out_bank_stride, out_row_stride};
+  if (out_ranks == nullptr) return kErrShape;
+  return sparse_step_impl(q_reordered, k_reordered, v_transposed, partition, k_norm_max, banks, S, D, n_video, scale,
+                          coarse_out, coarse_lse, detail_value, detail_log_mass, old_lse, center, out_pos, nullptr,
+                          status, stream, &sink);
 }
 
 int recap_exp2_check(const float* in, float* out, int n, void* stream) {
@@ -481,6 +607,54 @@ int recap_refresh_detail_noalloc(const void* full_o, const float* full_lse, cons
   a.partials = nullptr;
   a.stats = stats;
   return launch_refresh_noalloc(a, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------- buffers shared between ranks
+
+int recap_peer_alloc(int64_t bytes, void** ptr) {
+  if (bytes <= 0 || ptr == nullptr) return kErrShape;
+  return cudaMalloc(ptr, static_cast<size_t>(bytes)) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int recap_peer_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? kOk : kErrLaunch; }
+
+int recap_peer_handle_bytes(void) { return static_cast<int>(sizeof(cudaIpcMemHandle_t)); }
+
+int recap_peer_export(void* ptr, void* handle_out) {
+  if (ptr == nullptr || handle_out == nullptr) return kErrShape;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) return kErrLaunch;
+  std::memcpy(handle_out, &h, sizeof(h));
+  return kOk;
+}
+
+int recap_peer_import(const void* handle, void** ptr) {
+  if (handle == nullptr || ptr == nullptr) return kErrShape;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int recap_peer_close(void* ptr) { return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? kOk : kErrLaunch; }
+
+int recap_scatter_rows(const void* src, int banks, int S, int D, void* const* out_ranks, int n_ranks,
+                       int tokens_per_rank, int64_t out_bank_stride, int64_t out_row_stride, void* stream) {
+  if (src == nullptr || out_ranks == nullptr || banks <= 0 || S <= 0 || (D != 64 && D != 128) ||
+      n_ranks < 1 || n_ranks > kMaxRanks || static_cast<int64_t>(n_ranks) * tokens_per_rank != S ||
+      out_bank_stride < 0 || out_row_stride < D)
+    return kErrShape;
+  const size_t row = static_cast<size_t>(D) * 2;
+  for (int q = 0; q < n_ranks; ++q) {
+    if (out_ranks[q] == nullptr) return kErrShape;
+    for (int b = 0; b < banks; ++b) {
+      const uint8_t* s = static_cast<const uint8_t*>(src) + (static_cast<size_t>(b) * S + static_cast<size_t>(q) * tokens_per_rank) * row;
+      uint8_t* d = static_cast<uint8_t*>(out_ranks[q]) + static_cast<size_t>(b) * out_bank_stride * 2;
+      if (cudaMemcpy2DAsync(d, static_cast<size_t>(out_row_stride) * 2, s, row, row, tokens_per_rank,
+                            cudaMemcpyDefault, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return kErrLaunch;
+    }
+  }
+  return kOk;
 }
 
 }  // extern "C"

@@ -111,6 +111,17 @@ struct Item {
   int bank, qa, qb;
 };
 
+// Output row of bank `bank` at native position `pos` (in the caller's buffer, or in the token
+// shard of the rank that holds `pos`).
+__device__ __forceinline__ __nv_bfloat16* out_row(const FmhaArgs& a, int bank, int pos) {
+  if (a.n_ranks > 1) {
+    const int q = pos / a.tokens_per_rank;
+    return a.o_rank[q] + static_cast<int64_t>(bank) * a.o_bank_stride +
+           static_cast<int64_t>(pos - q * a.tokens_per_rank) * a.o_row_stride;
+  }
+  return a.o + static_cast<int64_t>(bank) * a.o_bank_stride + static_cast<int64_t>(pos) * a.o_row_stride;
+}
+
 __device__ __forceinline__ Item decode_item(const FmhaArgs& a, int b) {
   Item it;
   const int NB = a.NB;
@@ -733,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = 1.f / l_run;
       const float lse_h = (m_run + __log2f(l_run)) * 0.69314718055994531f;
       const size_t bank_rows = static_cast<size_t>(it.bank) * args.S;
-      __nv_bfloat16* orow = args.o + (bank_rows + pos) * D;
+      __nv_bfloat16* orow = out_row(args, it.bank, pos);
       if (staged) {
         // corrected merge (recap/kernels/detail_cache.py:267-292)
         const float admit = expf(-fabsf(gl - ogl - cshift));
@@ -797,7 +808,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
                        : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
                        : "r"(s_go + (j >> 3) * (128 * 128) + ti * 128 + (((j & 7) ^ (ti & 7)) << 4)));
-          if (ok_i) st_stream_v4(args.o + (bank_rows + pos_i) * D + j * 8, make_uint4(w0, w1, w2, w3));
+          if (ok_i) st_stream_v4(out_row(args, it.bank, pos_i) + j * 8, make_uint4(w0, w1, w2, w3));
         }
       } else {
 #pragma unroll 1
@@ -822,6 +833,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (in_seq && args.lse) args.lse[bank_rows + pos] = lse_h;
     }
   }
+  // Rows stored into other ranks' shards are made visible beyond this GPU before the kernel
+  // ends (the ranks then meet at a collective before reading them).
+  if (args.n_ranks > 1) __threadfence_system();
   // Nothing asynchronous is in flight past this barrier, on the normal path and after an
   // abort alike: the producer waited (bounded) for the completion of every TMA load it
   // issued - at most NST can be outstanding, since each load into a slot first waited for

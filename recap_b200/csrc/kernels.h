@@ -10,6 +10,10 @@
 
 namespace recap {
 
+// Largest number of ranks whose buffers one launch reads from or writes to directly
+// (the token shards of a sequence-parallel layer, over NVLink peer mappings).
+constexpr int kMaxRanks = 8;
+
 // Host-side status codes (the C ABI returns them).
 enum : int {
   kOk = 0,
@@ -39,6 +43,10 @@ struct GatherArgs {
   __nv_bfloat16* variance_bf16; // [banks, nB_pad, D] (nullable)
   float* k_norm_max;            // [banks, NB] largest |k| over the tokens of each block (nullable)
   float* k_mean_norm;           // [banks, nB] |bf16(kbar)| of each video block (nullable)
+  // n_ranks > 1: native token n is row n - q tokens_per_rank of rank q = n / tokens_per_rank,
+  // whose tensor t starts at rank_src[q][t] (same strides); src[t] is then rank_src[0][t]
+  int n_ranks, tokens_per_rank;
+  const __nv_bfloat16* rank_src[kMaxRanks][3];
 };
 int launch_gather(const GatherArgs& a, cudaStream_t s);
 int gather_max_rank();
@@ -160,6 +168,12 @@ struct FmhaArgs {
   const float* ogl;        // [banks, rows] coarse LSE at the refresh
   const float* center;     // [banks]
   int tma_epilogue;        // 1: tm_go / tm_det describe go / det (epilogue 1 with video rows)
+  // Output rows: bank b, native position n at o + b o_bank_stride + n o_row_stride (elements;
+  // S D and D for a [banks, S, D] output).  n_ranks > 1: at o_rank[q] + b o_bank_stride +
+  // (n - q tokens_per_rank) o_row_stride with q = n / tokens_per_rank (token shards of ranks)
+  int64_t o_bank_stride, o_row_stride;
+  int n_ranks, tokens_per_rank;
+  __nv_bfloat16* o_rank[kMaxRanks];
   const __nv_bfloat16* q;  // [banks, S_pad, D] reordered Q (the tiles tm_q reads; L2 prefetch)
   int num_sms;             // SMs of the device: the CTA that follows this one on its SM
   int* status;

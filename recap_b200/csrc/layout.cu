@@ -160,13 +160,20 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
     }
     nat[p] = n;
   }
+  // Address of this thread's chunk of native token n of tensor t: in the one source, or in
+  // the token shard of the rank that holds n.
+  auto row_src = [&](int t, int n) -> const __nv_bfloat16* {
+    const int64_t off = bi * a.stride_b[t] + hi * a.stride_h[t] + ch * 8;
+    if (a.n_ranks > 1) {
+      const int q = n / a.tokens_per_rank;
+      return a.rank_src[q][t] + off + static_cast<int64_t>(n - q * a.tokens_per_rank) * a.stride_s[t];
+    }
+    return a.src[t] + off + static_cast<int64_t>(n) * a.stride_s[t];
+  };
   auto load_rows = [&](int t, uint4 (&v)[PASSES]) {
-    const __nv_bfloat16* src = a.src[t];
-    if (src == nullptr) return;
-    const __nv_bfloat16* base = src + bi * a.stride_b[t] + hi * a.stride_h[t] + ch * 8;
+    if (a.src[t] == nullptr) return;
 #pragma unroll
-    for (int p = 0; p < PASSES; ++p)
-      v[p] = nat[p] >= 0 ? ld_stream_v4(base + static_cast<int64_t>(nat[p]) * a.stride_s[t]) : make_uint4(0, 0, 0, 0);
+    for (int p = 0; p < PASSES; ++p) v[p] = nat[p] >= 0 ? ld_stream_v4(row_src(t, nat[p])) : make_uint4(0, 0, 0, 0);
   };
   float knorm2 = 0.f;  // largest |k|^2 over this thread's rows
   auto process = [&](int t, const uint4 (&v)[PASSES]) {
@@ -239,14 +246,11 @@ __global__ void __launch_bounds__(kThreads, 2) gather_kernel(const GatherArgs a)
     // is stored from there.  K and V are read back from shared memory for their stores,
     // pools and norms.
     auto copy_rows = [&](int t, uint8_t* tile) {
-      const __nv_bfloat16* src = a.src[t];
-      if (src == nullptr) return;
-      const __nv_bfloat16* base = src + bi * a.stride_b[t] + hi * a.stride_h[t] + ch * 8;
+      if (a.src[t] == nullptr) return;
 #pragma unroll
       for (int p = 0; p < PASSES; ++p) {
         const bool in = nat[p] >= 0;
-        cp_async16(smem_u32(tile + stage_off<D>(p * RPP + rsub, ch)),
-                   in ? base + static_cast<int64_t>(nat[p]) * a.stride_s[t] : base, in ? 16u : 0u);
+        cp_async16(smem_u32(tile + stage_off<D>(p * RPP + rsub, ch)), row_src(t, in ? nat[p] : 0), in ? 16u : 0u);
       }
     };
     auto read_rows = [&](const uint8_t* tile, uint4 (&v)[PASSES]) {

@@ -257,6 +257,24 @@ class Operator:
             out = self._refresh(layer, bank, query, key, value)
         return out if in_dtype == torch.bfloat16 else out.to(in_dtype)
 
+    @torch.no_grad()
+    def attend_sharded(self, layer_index: int, io) -> None:
+        """One REFRESH or SPARSE call of a sequence-parallel layer whose Q/K/V projections and
+        attention output stay sharded by token over the ranks (``recap_b200.ulysses.ShardedIO``):
+        the layout pass reads this rank's heads from every rank's projection buffer, and the
+        output rows go to the ranks that own the tokens.  The same arithmetic as ``attend``
+        on the gathered heads; the caller orders the ranks' buffer writes around it (a
+        collective before and after)."""
+        if self.kind not in (REFRESH, SPARSE):
+            raise ValueError("sharded attention runs REFRESH and SPARSE calls")
+        layer = self.layers[self.stream][layer_index]
+        bank = self.banks[self.stream][layer_index]
+        if self.kind == SPARSE:
+            self._sparse(layer, bank, None, None, None, io=io)
+        else:
+            out = self._refresh(layer, bank, None, None, None, io=io)
+            io.scatter_output(out)
+
     def _scale(self, query: torch.Tensor) -> float:
         return 1.0 / math.sqrt(query.shape[-1])
 
@@ -326,7 +344,7 @@ class Operator:
         return layer_counts_reduce(counts, self.process_group)
 
     @torch.no_grad()
-    def _refresh(self, layer: SparseAttention, bank: DetailBank, query, key, value) -> torch.Tensor:
+    def _refresh(self, layer: SparseAttention, bank: DetailBank, query, key, value, io=None) -> torch.Tensor:
         """Dense output; stores the refinement and measures the previous one
         (recap/operator.py:331-473).
 
@@ -337,10 +355,12 @@ class Operator:
         tail score the old refinement and, when the partition is kept, also give the new
         one, so one pass over every key block yields the dense output and that head.  Only
         a re-selection needs a second head pass, under the new partition."""
+        if io is not None:
+            query = io.shape_carrier()
         scale = self._scale(query)
-        dev = query.device
+        dev = query.device if io is None else io.device
         status = self.status_word(dev)
-        inputs = layer.prepare(query, key, value, q_mean=True)
+        inputs = layer.prepare(query, key, value, q_mean=True, shards=io)
         sh = inputs.shapes
         if bank.valid and not _bank_fits(bank, sh):
             # A refinement of another shape cannot be scored against this call (the
@@ -403,15 +423,17 @@ class Operator:
     # -- sparse ----------------------------------------------------------------------------
 
     @torch.no_grad()
-    def _sparse(self, layer: SparseAttention, bank: DetailBank, query, key, value) -> torch.Tensor:
+    def _sparse(self, layer: SparseAttention, bank: DetailBank, query, key, value, io=None) -> torch.Tensor | None:
         """Head computed exactly, plus coarse tail and weighted cached refinement
         (recap/operator.py:478-527)."""
         if not bank.valid or bank.partition is None:
             raise RuntimeError("a sparse call was requested before an exact refresh")
+        if io is not None:
+            query = io.shape_carrier()
         scale = self._scale(query)
-        dev = query.device
+        dev = query.device if io is None else io.device
         status = self.status_word(dev)
-        inputs = layer.prepare(query, key, value, q_mean=False)
+        inputs = layer.prepare(query, key, value, q_mean=False, shards=io)
         sh = inputs.shapes
         if bank.partition.shape != (sh.batch, sh.heads, sh.nB, sh.nB):
             raise ValueError("the cached partition does not match this call's shape")
@@ -419,15 +441,17 @@ class Operator:
         coarse, coarse_lse, center = layer.coarse_tail_apply(
             inputs, context, bank.partition, scale, old_lse=bank.coarse_lse, status=status
         )
+        common = (_lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(bank.partition),
+                  _lib.ptr(inputs.k_norm_max), sh.banks, sh.S, sh.D, sh.n_video, float(scale), _lib.ptr(coarse),
+                  _lib.ptr(coarse_lse), _lib.ptr(bank.value), _lib.ptr(bank.log_mass), _lib.ptr(bank.coarse_lse),
+                  _lib.ptr(center), _lib.ptr(gather_rows(self.layout, dev)))
+        if io is not None:
+            # the epilogue stores every row into the shard of the rank that owns its token
+            self.launches.run("recap_sparse_step_ranks", 1, *common, *io.output_sinks(), _lib.ptr(status),
+                              _lib.stream_handle(dev))
+            return None
         out = torch.empty(sh.batch, sh.heads, sh.S, sh.D, dtype=torch.bfloat16, device=dev)
-        self.launches.run(
-            "recap_sparse_step", 1,
-            _lib.ptr(inputs.q), _lib.ptr(inputs.k), _lib.ptr(inputs.v_t), _lib.ptr(bank.partition),
-            _lib.ptr(inputs.k_norm_max), sh.banks,
-            sh.S, sh.D, sh.n_video, float(scale), _lib.ptr(coarse), _lib.ptr(coarse_lse), _lib.ptr(bank.value),
-            _lib.ptr(bank.log_mass), _lib.ptr(bank.coarse_lse), _lib.ptr(center),
-            _lib.ptr(gather_rows(self.layout, dev)), _lib.ptr(out), _lib.ptr(status), _lib.stream_handle(dev),
-        )
+        self.launches.run("recap_sparse_step", 1, *common, _lib.ptr(out), _lib.ptr(status), _lib.stream_handle(dev))
         return out
 
     # -- the refinement error --------------------------------------------------------------

@@ -176,14 +176,20 @@ class SparseAttention:
         *,
         q_mean: bool,
         means: bool = True,
+        shards=None,
     ) -> LayerInputs:
+        """One layout pass.  ``shards`` (a ``recap_b200.ulysses.ShardedIO``): Q, K and V are the
+        token shards of the ranks of a sequence-parallel layer, read in place over NVLink;
+        ``query``, ``key`` and ``value`` are then unused."""
         layout = self.geometry.layout
+        if shards is not None:
+            query = shards.shape_carrier()
         if query.shape[-2] != sequence_tokens(layout):
             raise ValueError(
                 f"sequence {query.shape[-2]} != video+text {sequence_tokens(layout)}"
             )
         sh = Shapes.of(query, layout.video_tokens)
-        dev = query.device
+        dev = query.device if shards is None else shards.device
         bf = torch.bfloat16
         q_r = torch.empty(sh.banks, sh.S_pad, sh.D, dtype=bf, device=dev)
         k_r = torch.empty_like(q_r)
@@ -206,11 +212,16 @@ class SparseAttention:
                 basis = self._basis
                 var = torch.empty(sh.banks, sh.nB, sh.D, dtype=f32, device=dev)
                 var_bf16 = torch.zeros(sh.banks, sh.nB_pad, sh.D, dtype=bf, device=dev)
-        strides = _strides3(query, key, value)
+        if shards is not None:
+            qr, kr, vr, n_ranks, tpr, strides = shards.gather_sources()
+            entry = ("recap_layout_gather_ranks", qr, kr, vr, n_ranks, tpr, strides, sh.heads)
+        else:
+            strides = _strides3(query, key, value)
+            entry = ("recap_layout_gather", _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), strides, sh.batch,
+                     sh.heads)
         self.launches.run(
-            "recap_layout_gather", 1,
-            _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), strides,
-            sh.batch, sh.heads, sh.S, sh.D, sh.n_video, _lib.ptr(gather_rows(layout, dev)),
+            entry[0], 1, *entry[1:],
+            sh.S, sh.D, sh.n_video, _lib.ptr(gather_rows(layout, dev)),
             _lib.ptr(q_r), _lib.ptr(k_r), _lib.ptr(v_t), _lib.ptr(qm), _lib.ptr(km), _lib.ptr(vm),
             _lib.ptr(kmb), _lib.ptr(vmtb), _lib.ptr(kct), _lib.ptr(basis), rank if basis is not None else 0,
             _lib.ptr(var), _lib.ptr(var_bf16), _lib.ptr(knm), _lib.ptr(kmn), _lib.stream_handle(dev),

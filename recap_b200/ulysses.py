@@ -74,3 +74,148 @@ def heads_to_seq(out: torch.Tensor, world: int, group=None) -> torch.Tensor:
     send = out[0].reshape(h, world, s, d).permute(1, 2, 0, 3).contiguous()  # [P, s, h, d]
     recv = _exchange(send, group)  # [P (head group), s, h, d]
     return recv.permute(1, 0, 2, 3).reshape(s, world * h * d)
+
+
+# ----------------------------------------------------------------------------- in place over NVLink
+
+
+class PeerBuffer:
+    """``nbytes`` of device memory on every rank of ``group`` (one process per GPU), each rank
+    holding the address of every rank's buffer: allocated by ``recap_peer_alloc`` and shared
+    by CUDA IPC handles exchanged over the process group.  ``close()`` (collective) releases
+    the mappings and the memory."""
+
+    def __init__(self, nbytes: int, group, device: torch.device):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        lib = _lib.load()
+        self.device = device
+        self.nbytes = int(nbytes)
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        own = ctypes.c_void_p()
+        _lib.check(lib.recap_peer_alloc(self.nbytes, ctypes.byref(own)), "recap_peer_alloc")
+        handle = ctypes.create_string_buffer(lib.recap_peer_handle_bytes())
+        _lib.check(lib.recap_peer_export(own, handle), "recap_peer_export")
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.ptrs: list[int] = []
+        for q, h in enumerate(handles):
+            if q == self.rank:
+                self.ptrs.append(int(own.value))
+                continue
+            p = ctypes.c_void_p()
+            _lib.check(lib.recap_peer_import(ctypes.create_string_buffer(h, len(h)), ctypes.byref(p)),
+                       "recap_peer_import")
+            self.ptrs.append(int(p.value))
+
+    def local(self, shape, dtype: torch.dtype) -> torch.Tensor:
+        """A tensor over this rank's buffer (no copy)."""
+        return _tensor_at(self.ptrs[self.rank], shape, dtype, self.device)
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if not self.ptrs:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank reads or writes another's buffer any more
+        lib = _lib.load()
+        for q, p in enumerate(self.ptrs):
+            if q != self.rank:
+                _lib.check(lib.recap_peer_close(p), "recap_peer_close")
+        dist.barrier(group=self.group)  # every mapping of this rank's buffer is closed
+        _lib.check(lib.recap_peer_free(self.ptrs[self.rank]), "recap_peer_free")
+        self.ptrs = []
+
+
+class _CudaView:
+    def __init__(self, ptr: int, numel: int):
+        self.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<i2", "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
+
+
+def _tensor_at(ptr: int, shape, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A tensor of 2-byte elements at a device address this process can reach (its own or an
+    imported peer buffer)."""
+    if torch.empty(0, dtype=dtype).element_size() != 2:
+        raise ValueError("2-byte element types only")
+    numel = 1
+    for n in shape:
+        numel *= int(n)
+    with torch.cuda.device(device):
+        flat = torch.as_tensor(_CudaView(ptr, numel), device=device)
+    return flat.view(dtype).view(*shape)
+
+
+class ShardedIO:
+    """The operands of one sequence-parallel attention call, left where the ranks hold them:
+    rank q's projection output ``[s, 3, H, d]`` (bf16) in ``qkv.ptrs[q]`` and its attention
+    output ``[s, H, d]`` in ``out.ptrs[q]``.  This rank attends on heads
+    ``[head0, head0 + heads)``: the layout pass reads their Q, K, V rows from every rank's
+    projection buffer, and the SPARSE step's epilogue stores every output row into the
+    buffer of the rank that owns the token."""
+
+    def __init__(self, qkv: PeerBuffer, out: PeerBuffer, total_heads: int, dim: int, seq: int):
+        world, rank = qkv.world, qkv.rank
+        self.tokens_per_rank, self.heads = check_split(seq, total_heads, world)
+        self.qkv, self.out = qkv, out
+        self.world, self.rank = world, rank
+        self.total_heads, self.dim, self.seq = total_heads, dim, seq
+        self.head0 = rank * self.heads
+        self.device = qkv.device
+        need_qkv = self.tokens_per_rank * 3 * total_heads * dim * 2
+        need_out = self.tokens_per_rank * total_heads * dim * 2
+        if qkv.nbytes < need_qkv or out.nbytes < need_out:
+            raise ValueError("peer buffers smaller than the token shards")
+
+    def shape_carrier(self) -> torch.Tensor:
+        """A shape-only ``[1, heads, S, d]`` tensor (the layer call's geometry)."""
+        return torch.empty(1, self.heads, self.seq, self.dim, device="meta")
+
+    def local_qkv(self) -> torch.Tensor:
+        return self.qkv.local((self.tokens_per_rank, 3, self.total_heads, self.dim), torch.bfloat16)
+
+    def local_out(self) -> torch.Tensor:
+        return self.out.local((self.tokens_per_rank, self.total_heads * self.dim), torch.bfloat16)
+
+    def gather_sources(self):
+        """Arguments of ``recap_layout_gather_ranks``: per-rank addresses of head ``head0`` of
+        Q, K and V, the rank count, tokens per rank and the element strides."""
+        import ctypes
+
+        H, d = self.total_heads, self.dim
+        arrs = []
+        for t in range(3):
+            off = (t * H + self.head0) * d * 2
+            arrs.append((ctypes.c_void_p * self.world)(*[p + off for p in self.qkv.ptrs]))
+        row = 3 * H * d
+        strides = (ctypes.c_int64 * 9)(*([self.seq * row, d, row] * 3))
+        return arrs[0], arrs[1], arrs[2], self.world, self.tokens_per_rank, strides
+
+    def output_sinks(self):
+        """Arguments of the ``*_ranks`` attention passes: per-rank addresses of head
+        ``head0`` of token 0, rank count, tokens per rank, bank and row strides."""
+        import ctypes
+
+        d = self.dim
+        ptrs = (ctypes.c_void_p * self.world)(*[p + self.head0 * d * 2 for p in self.out.ptrs])
+        return ptrs, self.world, self.tokens_per_rank, d, self.total_heads * d
+
+    def scatter_output(self, out: torch.Tensor) -> None:
+        """Store a contiguous ``[1, heads, S, d]`` attention output computed locally into the
+        ranks' output buffers (copy-engine peer copies over NVLink)."""
+        from . import _lib
+
+        if not out.is_contiguous() or tuple(out.shape) != (1, self.heads, self.seq, self.dim):
+            raise ValueError("scatter_output takes this rank's contiguous [1, heads, S, d] output")
+        ptrs, n, tpr, bank_stride, row_stride = self.output_sinks()
+        _lib.call("recap_scatter_rows", _lib.ptr(out), self.heads, self.seq, self.dim, ptrs, n, tpr, bank_stride,
+                  row_stride, _lib.stream_handle(out.device))
