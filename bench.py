@@ -373,6 +373,38 @@ def workload_config(w: dict, world: int) -> dict:
             "l2": f"inputs {in_gb:.2f} GB per step > 126 MB L2 (no flush needed)"}
 
 
+def selection_roofline(w: dict, n_heads: int, refresh_times: dict, hbm_gbs: float) -> dict:
+    """HBM figures of the selection at a REFRESH (this rank's banks).  B_sel counts the
+    algorithmic bytes of pooling and top-k: the Q and K video rows read once (bf16), the
+    pooled means written (fp32) and the kept indices (4 bytes each).  The pooling runs
+    inside the layout pass, which also writes the reordered operands of the attention
+    kernels, so B_sel over gather + select time is a lower bound of the selection's rate;
+    the layout pass's own bytes and rate are reported beside it."""
+    nv = w["grid"][0] * w["grid"][1] * w["grid"][2]
+    S = nv + w["text"]
+    d = w["dim"]
+    banks = n_heads * w["batch"]
+    nb = (nv + 127) // 128
+    keep = max(1, round(w["density"] * nb))
+    s_pad = 128 * ((S + 127) // 128)
+    b_sel = 2 * banks * nv * d * 2 + 2 * banks * nb * d * 4 + banks * nb * keep * 4
+    t_g = sum(refresh_times.get("recap_layout_gather", [0.0]))
+    t_s = sum(refresh_times.get("recap_pool_select", [0.0]))
+    # layout pass: read Q, K, V native; write Q, K, V^T and the centred K^T (bf16), the
+    # three pooled means and the bf16 mean copies
+    b_gather = 3 * banks * S * d * 2 + 4 * banks * s_pad * d * 2 + 3 * banks * nb * d * 4
+    out = {"algorithmic_bytes": b_sel, "kernels_ms": {"recap_layout_gather": round(t_g, 4),
+                                                      "recap_pool_select": round(t_s, 4)},
+           "peak_gbs": hbm_gbs, "gather_pass_bytes": b_gather}
+    if t_g + t_s > 0:
+        out["achieved_gbs"] = round(b_sel / ((t_g + t_s) * 1e-3) / 1e9, 1)
+        out["frac"] = round(out["achieved_gbs"] / hbm_gbs, 4)
+    if t_g > 0:
+        out["gather_pass_gbs"] = round(b_gather / (t_g * 1e-3) / 1e9, 1)
+        out["gather_pass_frac"] = round(out["gather_pass_gbs"] / hbm_gbs, 4)
+    return out
+
+
 def parity_leg(w: dict, layout, hx: dict, basis, part0, part2, keep: bool, out_rows: dict, oracle_qblocks) -> dict:
     """The last timed SPARSE output of the sampled banks against the block oracle on the
     CPU (oracle/block_oracle.py), replaying the REFRESH on x0, the revalidating REFRESH on
@@ -577,6 +609,7 @@ def run_ours(args) -> None:
             "refresh_us": round(refresh_ms * 1000.0, 1),
             "refresh_kernels_ms": {k: round(sum(v), 4) for k, v in refresh_times.items()},
             "refresh_rerank": not keep,
+            "selection": selection_roofline(w, len(hs), refresh_times, pk["hbm_gbs"]),
             "kernels_ms": {k: round(v, 4) for k, v in kernels_ms.items()},
             "roofline": {
                 "kernel": "recap_sparse_step (block-sparse FMHA + corrected merge)",
