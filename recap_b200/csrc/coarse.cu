@@ -42,6 +42,10 @@
 // S2(j+1) and the products of the previous tile run while it computes.
 // The epilogue also writes the per-block sum of (lse - old_lse) for the drift centre
 // (recap/operator.py:148-150).
+// Two paths per tile: a tile whose logits provably stay within kBoundSlack of every row's
+// running max (|q| |kbar| bound, per warp) runs one pass (logit, gate, exponential, sums
+// and P per element); any other tile forms all its logits, exchanges the row maximum
+// between the two halves, rescales O if needed, then exponentiates.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -559,6 +563,83 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) ok = wait_all(bars.s2full, j & 1);
       if (!ok) break;
       tc_fence_after();
+      // A bounded tile keeps the running max of every row of the warp (by |q| and the tile's
+      // largest |kbar| its logits stay within kBoundSlack of it), so each logit is
+      // exponentiated as soon as it is formed: one pass over the sixteen-column steps, with
+      // the gate a predicate that serves the gated logit and the gated mass.  The arithmetic,
+      // its order and the four partial sums are those of the two-pass path below with
+      // alpha = 1 and an unchanged max, so the two give the same bits.
+      const bool bounded =
+          m_run != -INFINITY && __all_sync(0xffffffffu, qn_l2 * tile_kn[j] + bound_add <= m_run + kBoundSlack);
+      if (bounded) {
+        static_assert(kHalf / 16 >= 2, "S2 is released after the second-to-last step's loads");
+        const float neg_m = -m_run;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f}, gs[4] = {0.f, 0.f, 0.f, 0.f};
+        float sa1[16], sa2[16], sb1[16], sb2[16];
+        uint32_t pk[16];
+        tmem_ld16(t_s1 + b * kTileN + h * kHalf + lane_base, sa1);
+        tmem_ld16(t_s2 + h * kHalf + lane_base, sa2);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < kHalf / 16; ++k) {
+          float (&v1)[16] = (k & 1) ? sb1 : sa1;
+          float (&v2)[16] = (k & 1) ? sb2 : sa2;
+          if (k + 1 < kHalf / 16) {
+            float (&n1)[16] = (k & 1) ? sa1 : sb1;
+            float (&n2)[16] = (k & 1) ? sa2 : sb2;
+            tmem_ld16(t_s1 + b * kTileN + h * kHalf + (k + 1) * 16 + lane_base, n1);
+            tmem_ld16(t_s2 + h * kHalf + (k + 1) * 16 + lane_base, n2);
+          }
+          const float4* ct4 = reinterpret_cast<const float4*>(colterm + j * kTileN + h * kHalf + k * 16);
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const float4 ct = ct4[e4];
+            const float cts[4] = {ct.x, ct.y, ct.z, ct.w};
+#pragma unroll
+            for (int q2 = 0; q2 < 2; ++q2) {
+              const int el = 4 * e4 + 2 * q2;      // first element of the pair in this step
+              const int i = (k & 1) * 8 + el / 2;  // the pair's index in its 32-column chunk
+              float y[2];
+              bool gated[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const float quad = v2[el + u];
+                const float base = fmaf(v1[el + u], s_l2, cts[2 * q2 + u]);
+                gated[u] = quad <= gate_max;
+                y[u] = gated[u] ? fmaf(quad, h_l2, base) : base;
+              }
+              add2(y[0], y[1], neg_m, neg_m);
+              float p0, p1;
+              if ((kCoarsePolyPairs >> i) & 1u) {
+                exp2_poly2(p0, p1, y[0], y[1]);
+              } else {
+                p0 = fast_exp2(y[0]);
+                p1 = fast_exp2(y[1]);
+              }
+              add2(ls[(i & 1) * 2], ls[(i & 1) * 2 + 1], p0, p1);
+              if (gated[0]) gs[(i & 1) * 2] += p0;
+              if (gated[1]) gs[(i & 1) * 2 + 1] += p1;
+              pk[i] = pack_bf16(p0, p1);
+            }
+          }
+          // P of blocks 64h + 32c .. + 31 (c = k / 2) into columns whose S1 values were read
+          if (k & 1) tmem_st16(t_s1 + b * kTileN + h * kHalf + (k >> 1) * 16 + lane_base, pk);
+          if (k + 1 < kHalf / 16) tmem_wait_ld();  // the next step's columns have landed
+          if (k == kHalf / 16 - 2) {
+            // every S2 column of this tile is in registers: the next quadratic term may go
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bars.s2free);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bars.pfull + b);
+        l_run = l_run + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+        g_run = g_run + ((gs[0] + gs[1]) + (gs[2] + gs[3]));
+        continue;
+      }
       float x[kHalf];
       uint32_t gate[2];
       uint32_t one;  // 1, opaque to the compiler: the mask bits below stay multiply-adds
@@ -618,9 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bars.s2free);
       float alpha = 1.f;
       bool rescale = false;
-      const bool bounded =
-          m_run != -INFINITY && __all_sync(0xffffffffu, qn_l2 * tile_kn[j] + bound_add <= m_run + kBoundSlack);
-      if (!bounded) {
+      {
         float mx[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx[k] = max3(x[k], x[8 + k], x[16 + k]);
