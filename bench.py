@@ -72,9 +72,11 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default=WORKLOAD["name"],
                    help="BASELINE config 4 (default), 2 or 3")
-    p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
-                   help="stack workload: the Ulysses exchange fused into the layout pass and the attention "
-                        "epilogue over NVLink peer memory (p2p), or NCCL all_to_all_single around the call")
+    p.add_argument("--exchange", choices=["push", "p2p", "nccl"], default="push",
+                   help="stack workload, the Ulysses exchange: copy-engine peer writes of the projections into "
+                        "the owners' receive buffers and the attention epilogue storing rows into the owners' "
+                        "shards (push); the layout pass reading the ranks' projections in place over NVLink "
+                        "(p2p); or NCCL all_to_all_single around the call (nccl)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true", help="skip the CPU oracle check of the last timed output")
@@ -699,18 +701,28 @@ class AttentionStack:
         self.timing = False
         self.events: list[list] = []
         self.io = None
-        if self.exchange == "p2p":
-            # the projection output and the attention output of every rank, reachable by all
-            self.peer_qkv = PeerBuffer(self.s * 3 * hd * 2, group, device)
+        self.peers: list = []
+        if self.exchange in ("p2p", "push"):
+            # the attention output of every rank, reachable by all; p2p: the projections too;
+            # push: each rank's receive buffer of its heads' projections
             self.peer_out = PeerBuffer(self.s * hd * 2, group, device)
-            self.io = ShardedIO(self.peer_qkv, self.peer_out, self.heads, self.dim, self.S)
+            self.peers.append(self.peer_out)
+            if self.exchange == "p2p":
+                self.peer_qkv = PeerBuffer(self.s * 3 * hd * 2, group, device)
+                self.peers.append(self.peer_qkv)
+                self.io = ShardedIO(self.peer_qkv, self.peer_out, self.heads, self.dim, self.S)
+            else:
+                self.peer_recv = PeerBuffer(self.S * 3 * self.h * self.dim * 2, group, device)
+                self.peers.append(self.peer_recv)
+                self.qkv_local = torch.empty(self.s, 3, self.heads, self.dim, dtype=bf, device=device)
+                self.io = ShardedIO(None, self.peer_out, self.heads, self.dim, self.S, recv=self.peer_recv)
             self.flag = torch.zeros(1, device=device)
 
     def close(self) -> None:
-        if self.io is not None:
-            self.peer_qkv.close()
-            self.peer_out.close()
-            self.io = None
+        for p in self.peers:
+            p.close()
+        self.peers = []
+        self.io = None
 
     def _meet(self) -> None:
         """Every rank's writes so far are done before any rank goes on (a one-element
@@ -755,14 +767,19 @@ class AttentionStack:
         over NVLink, and the attention epilogue stores each output row into the shard of
         the rank that owns the token."""
         io = self.io
-        qkv = io.local_qkv().view(self.s, 3 * self.heads * self.dim)
+        push = self.exchange == "push"
+        qkv4 = self.qkv_local if push else io.local_qkv()
+        qkv = qkv4.view(self.s, 3 * self.heads * self.dim)
         y = io.local_out()
         for layer in range(len(self.w_qkv)):
             marks: list = []
             self._mark(marks)
             torch.matmul(x, self.w_qkv[layer], out=qkv)
             self._mark(marks)
-            self._meet()  # every shard written before any rank reads
+            if push:
+                # the owners finished reading their receive buffers before the last meeting
+                io.push(qkv4)
+            self._meet()  # every shard written (pushed) before any rank reads
             self._mark(marks)
             self.op.attend_sharded(layer, io)
             self._mark(marks)
@@ -838,8 +855,11 @@ def run_stack(args, w: dict, world: int, rank: int, dev, group) -> None:
             sparse_ms = timed(SPARSE, args.steps, step)
         gpu_launches = op.launches.count - launches_before
         step += args.steps
+        op.launches.timing = True
         timed(SPARSE, 1, step, phases=True)
         phases = stack.take_phases()
+        ktimes = {k: sum(v) for k, v in op.launches.take_times().items()}
+        op.launches.timing = False
         op.check_device_status()
         stack.close()
     total = sum(phases.values())
@@ -865,9 +885,13 @@ def run_stack(args, w: dict, world: int, rank: int, dev, group) -> None:
                         f"{n_refresh} x REFRESH + {w['schedule_steps'] - n_refresh} x SPARSE, from the measured steps",
             "phases_ms_per_step": {k: round(v, 3) for k, v in phases.items()},
             "all_to_all_share": round(a2a / total, 4) if total else None,
-            "exchange_phases": ("NCCL all_to_all_single with the layout copies around it" if stack.exchange == "nccl"
-                                else "the two one-element all-reduces that order the ranks' buffer writes; the "
-                                     "transfers themselves run inside the layout pass and the attention epilogue"),
+            "exchange_phases": {
+                "nccl": "NCCL all_to_all_single with the layout copies around it",
+                "push": "copy-engine peer writes of the projections plus the all-reduce that orders them; the "
+                        "output rows go to their owners from the attention epilogue (in 'attention')",
+                "p2p": "the two one-element all-reduces that order the ranks' buffer writes; the transfers "
+                       "themselves run inside the layout pass and the attention epilogue"}[stack.exchange],
+            "kernels_ms_per_step": {k: round(v, 3) for k, v in ktimes.items()},
             "gpu_launches": gpu_launches,
             "clocks": clk.summary(),
         }

@@ -304,6 +304,24 @@ int recap_peer_export(void* ptr, void* handle_out);
 int recap_peer_import(const void* handle, void** ptr);
 int recap_peer_close(void* ptr);
 
+/* The sequence-to-head exchange of a sequence-parallel layer as peer stores: rank `rank` of
+ * n_ranks writes its projections src [tokens, 3, heads, D] bf16 (contiguous) into the receive
+ * buffer of the rank owning each head group, recv_ranks[q] [n_ranks tokens, 3, heads / n_ranks,
+ * D] (q's heads [q heads / n_ranks, (q + 1) heads / n_ranks)), at rows [rank tokens, (rank + 1)
+ * tokens); other ranks' buffers opened with recap_peer_import, writes crossing NVLink.  The
+ * caller orders the ranks around it (a collective on the stream before the owners read).  No
+ * counterpart in the reference (it exchanges with all-to-all collectives). */
+int recap_push_heads(const void* src, int tokens, int heads, int D, int rank, int n_ranks,
+                     void* const* recv_ranks, void* stream);
+
+/* `height` rows of `width` bytes from src (row pitch src_pitch bytes) to dst (dst_pitch), by a
+ * copy engine (cudaMemcpy2DAsync; either side may be a peer buffer opened by recap_peer_import,
+ * crossing NVLink as peer writes or reads).  The push form of the Ulysses exchange: each rank
+ * writes its head groups' rows into the owners' receive buffers.  No counterpart in the
+ * reference. */
+int recap_copy_rows_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
+                       int64_t height, void* stream);
+
 /* Copy a [banks, S, D] bf16 output into the ranks' token shards as the *_ranks attention passes
  * place it (copy engines; peer copies over NVLink): the step after a REFRESH whose dense
  * output the refinement write reads locally.  No counterpart in the reference. */

@@ -21,7 +21,7 @@ LIB_PATH = PACKAGE_DIR / LIB_NAME
 BUILD_DIR = PACKAGE_DIR / "_build"
 
 SOURCES = ["layout.cu", "select.cu", "closure.cu", "cvk.cu", "coarse.cu", "fmha.cu", "refresh.cu", "selftest.cu",
-           "capi.cu"]
+           "exchange.cu", "capi.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",

@@ -637,6 +637,37 @@ int recap_peer_import(const void* handle, void** ptr) {
 
 int recap_peer_close(void* ptr) { return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? kOk : kErrLaunch; }
 
+int recap_push_heads(const void* src, int tokens, int heads, int D, int rank, int n_ranks,
+                     void* const* recv_ranks, void* stream) {
+  if (src == nullptr || recv_ranks == nullptr || tokens <= 0 || (D != 64 && D != 128) || n_ranks < 1 ||
+      n_ranks > kMaxRanks || heads <= 0 || heads % n_ranks || rank < 0 || rank >= n_ranks ||
+      (reinterpret_cast<uintptr_t>(src) & 15))
+    return kErrShape;
+  PushArgs a{};
+  a.tokens = tokens;
+  a.heads = heads;
+  a.heads_per_rank = heads / n_ranks;
+  a.D = D;
+  a.token0 = static_cast<int64_t>(rank) * tokens;
+  a.src = static_cast<const __nv_bfloat16*>(src);
+  for (int q = 0; q < n_ranks; ++q) {
+    if (recv_ranks[q] == nullptr || (reinterpret_cast<uintptr_t>(recv_ranks[q]) & 15)) return kErrShape;
+    a.dst[q] = static_cast<__nv_bfloat16*>(recv_ranks[q]);
+  }
+  return launch_push(a, static_cast<cudaStream_t>(stream));
+}
+
+int recap_copy_rows_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
+                       int64_t height, void* stream) {
+  if (dst == nullptr || src == nullptr || width <= 0 || height <= 0 || dst_pitch < width || src_pitch < width)
+    return kErrShape;
+  return cudaMemcpy2DAsync(dst, static_cast<size_t>(dst_pitch), src, static_cast<size_t>(src_pitch),
+                           static_cast<size_t>(width), static_cast<size_t>(height), cudaMemcpyDefault,
+                           static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? kOk
+             : kErrLaunch;
+}
+
 int recap_scatter_rows(const void* src, int banks, int S, int D, void* const* out_ranks, int n_ranks,
                        int tokens_per_rank, int64_t out_bank_stride, int64_t out_row_stride, void* stream) {
   if (src == nullptr || out_ranks == nullptr || banks <= 0 || S <= 0 || (D != 64 && D != 128) ||

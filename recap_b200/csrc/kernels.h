@@ -51,6 +51,15 @@ struct GatherArgs {
 int launch_gather(const GatherArgs& a, cudaStream_t s);
 int gather_max_rank();
 
+// ------------------------------------------------------------------ sequence-to-head exchange
+struct PushArgs {
+  int tokens, heads, heads_per_rank, D;  // this rank's tokens; heads of the layer
+  int64_t token0;                        // this rank's first token (its rows in the receive buffers)
+  const __nv_bfloat16* src;              // [tokens, 3, heads, D] this rank's projections
+  __nv_bfloat16* dst[kMaxRanks];         // [S, 3, heads_per_rank, D] receive buffer of each rank
+};
+int launch_push(const PushArgs& a, cudaStream_t s);
+
 // ------------------------------------------------------------------ C_vk on tensor cores
 struct CvkArgs {
   int banks, n_video, video_steps;  // video_steps = ceil(n_video / 64)

@@ -213,8 +213,7 @@ class SparseAttention:
                 var = torch.empty(sh.banks, sh.nB, sh.D, dtype=f32, device=dev)
                 var_bf16 = torch.zeros(sh.banks, sh.nB_pad, sh.D, dtype=bf, device=dev)
         if shards is not None:
-            qr, kr, vr, n_ranks, tpr, strides = shards.gather_sources()
-            entry = ("recap_layout_gather_ranks", qr, kr, vr, n_ranks, tpr, strides, sh.heads)
+            entry = shards.gather_call()
         else:
             strides = _strides3(query, key, value)
             entry = ("recap_layout_gather", _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), strides, sh.batch,

@@ -163,18 +163,26 @@ class ShardedIO:
     projection buffer, and the SPARSE step's epilogue stores every output row into the
     buffer of the rank that owns the token."""
 
-    def __init__(self, qkv: PeerBuffer, out: PeerBuffer, total_heads: int, dim: int, seq: int):
-        world, rank = qkv.world, qkv.rank
+    def __init__(self, qkv: PeerBuffer, out: PeerBuffer, total_heads: int, dim: int, seq: int,
+                 recv: PeerBuffer | None = None):
+        """``recv`` (push mode): each rank's receive buffer ``[S, 3, H/P, d]`` of its heads'
+        projections; ``push`` writes every rank's rows into it with copy-engine peer writes
+        and the layout pass then reads it locally.  Without it the layout pass reads the
+        ranks' projection buffers ``qkv`` in place."""
+        world, rank = out.world, out.rank
         self.tokens_per_rank, self.heads = check_split(seq, total_heads, world)
         self.qkv, self.out = qkv, out
         self.world, self.rank = world, rank
         self.total_heads, self.dim, self.seq = total_heads, dim, seq
         self.head0 = rank * self.heads
-        self.device = qkv.device
+        self.device = out.device
+        self.recv = recv
         need_qkv = self.tokens_per_rank * 3 * total_heads * dim * 2
         need_out = self.tokens_per_rank * total_heads * dim * 2
-        if qkv.nbytes < need_qkv or out.nbytes < need_out:
+        if (qkv is not None and qkv.nbytes < need_qkv) or out.nbytes < need_out:
             raise ValueError("peer buffers smaller than the token shards")
+        if recv is not None and recv.nbytes < seq * 3 * self.heads * dim * 2:
+            raise ValueError("receive buffer smaller than the heads' projections")
 
     def shape_carrier(self) -> torch.Tensor:
         """A shape-only ``[1, heads, S, d]`` tensor (the layer call's geometry)."""
@@ -185,6 +193,34 @@ class ShardedIO:
 
     def local_out(self) -> torch.Tensor:
         return self.out.local((self.tokens_per_rank, self.total_heads * self.dim), torch.bfloat16)
+
+    def push(self, qkv_local: torch.Tensor) -> None:
+        """Push mode: write this rank's ``[s, 3, H, d]`` projections of every head group into
+        the receive buffer of the rank that owns it, at this rank's token range: one kernel of
+        16-byte peer stores over NVLink (``recap_push_heads``)."""
+        import ctypes
+
+        from . import _lib
+
+        s, H, d = self.tokens_per_rank, self.total_heads, self.dim
+        if tuple(qkv_local.shape) != (s, 3, H, d) or not qkv_local.is_contiguous():
+            raise ValueError("push takes this rank's contiguous [s, 3, H, d] projections")
+        dst = (ctypes.c_void_p * self.world)(*self.recv.ptrs)
+        _lib.call("recap_push_heads", _lib.ptr(qkv_local), s, H, d, self.rank, self.world, dst,
+                  _lib.stream_handle(qkv_local.device))
+
+    def gather_call(self):
+        """The layout pass's entry point and its leading arguments (up to the head count)."""
+        import ctypes
+
+        if self.recv is not None:
+            h, d = self.heads, self.dim
+            base = self.recv.ptrs[self.rank]
+            row = 3 * h * d
+            strides = (ctypes.c_int64 * 9)(*([self.seq * row, d, row] * 3))
+            return ("recap_layout_gather", base, base + h * d * 2, base + 2 * h * d * 2, strides, 1, self.heads)
+        qr, kr, vr, n, tpr, strides = self.gather_sources()
+        return ("recap_layout_gather_ranks", qr, kr, vr, n, tpr, strides, self.heads)
 
     def gather_sources(self):
         """Arguments of ``recap_layout_gather_ranks``: per-rank addresses of head ``head0`` of

@@ -22,9 +22,13 @@ def _shards(full: torch.Tensor, world: int):
     return [full[q * s:(q + 1) * s].contiguous() for q in range(world)]
 
 
+@pytest.mark.parametrize("mode", ["in_place", "push"])
 @pytest.mark.parametrize("world,rank,text,text_first,d", [(2, 0, 64, False, 128), (2, 1, 64, False, 128),
                                                           (4, 2, 0, False, 64), (4, 3, 96, True, 128)])
-def test_sharded_attention_matches_plain(world, rank, text, text_first, d):
+def test_sharded_attention_matches_plain(world, rank, text, text_first, d, mode):
+    """``in_place``: the layout pass reads every rank's projection shard; ``push``: every
+    rank first writes its rows of this rank's heads into this rank's receive buffer
+    (``ShardedIO.push``, copy-engine copies) and the layout pass reads that locally."""
     from recap_b200 import REFRESH, SPARSE, Operator, OperatorConfig
     from recap_b200.sparse import Layout, SparseGeometry
     from recap_b200.ulysses import ShardedIO
@@ -44,6 +48,7 @@ def test_sharded_attention_matches_plain(world, rank, text, text_first, d):
     h = H // world
     head0 = rank * h
     out_bufs = [torch.zeros(s, H, d, dtype=torch.bfloat16, device=DEV) for _ in range(world)]
+    recv_bufs = [torch.zeros(S, 3, h, d, dtype=torch.bfloat16, device=DEV) for _ in range(world)]
     steps = [(0, REFRESH), (1, SPARSE), (2, REFRESH), (3, SPARSE)]
     base = torch.randn(S, 3, H, d, generator=g)
     for step, kind in steps:
@@ -54,7 +59,16 @@ def test_sharded_attention_matches_plain(world, rank, text, text_first, d):
                               device=torch.device(DEV), nbytes=min(nbytes))
         outp = SimpleNamespace(ptrs=[t.data_ptr() for t in out_bufs], world=world, rank=rank,
                                device=torch.device(DEV), nbytes=out_bufs[0].numel() * 2)
-        io = ShardedIO(qkv, outp, total_heads=H, dim=d, seq=S)
+        if mode == "push":
+            recv = SimpleNamespace(ptrs=[t.data_ptr() for t in recv_bufs], world=world, rank=rank,
+                                   device=torch.device(DEV), nbytes=recv_bufs[0].numel() * 2)
+            for src in range(world):  # every rank pushes its shard (emulated one after another)
+                src_out = SimpleNamespace(**{**vars(outp), "rank": src})
+                src_recv = SimpleNamespace(**{**vars(recv), "rank": src})
+                ShardedIO(None, src_out, total_heads=H, dim=d, seq=S, recv=src_recv).push(qkv_bufs[src])
+            io = ShardedIO(None, outp, total_heads=H, dim=d, seq=S, recv=recv)
+        else:
+            io = ShardedIO(qkv, outp, total_heads=H, dim=d, seq=S)
         assert io.head0 == head0 and io.heads == h
         q, k, v = (full[:, i, head0:head0 + h].permute(1, 0, 2).unsqueeze(0) for i in range(3))
         plain.begin_step(step, kind)
