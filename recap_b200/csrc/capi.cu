@@ -1,7 +1,8 @@
 // extern "C" entry points of librecap_b200.so (declared in include/recap_b200.h).
 // Each entry point checks its shapes, builds the TMA tensor maps it needs from the raw
 // device pointers, and launches on the given stream.  No entry point synchronises or
-// allocates device memory; scratch buffers are passed in by the caller.
+// allocates device memory (recap_peer_alloc, the allocator of buffers shared between ranks,
+// aside); scratch buffers are passed in by the caller.
 #include <cudaTypedefs.h>
 
 #include <mutex>
