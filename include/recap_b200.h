@@ -322,9 +322,10 @@ int recap_push_heads(const void* src, int tokens, int heads, int D, int rank, in
 int recap_copy_rows_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
                        int64_t height, void* stream);
 
-/* Copy a [banks, S, D] bf16 output into the ranks' token shards as the *_ranks attention passes
- * place it (copy engines; peer copies over NVLink): the step after a REFRESH whose dense
- * output the refinement write reads locally.  No counterpart in the reference. */
+/* Store a [banks, S, D] bf16 output (contiguous, 16-byte aligned) into the ranks' token shards
+ * as the *_ranks attention passes place it (one kernel of 16-byte peer stores over NVLink):
+ * the step after a REFRESH whose dense output the refinement write reads locally.  Strides
+ * are multiples of 8 elements.  No counterpart in the reference. */
 int recap_scatter_rows(const void* src, int banks, int S, int D, void* const* out_ranks, int n_ranks,
                        int tokens_per_rank, int64_t out_bank_stride, int64_t out_row_stride, void* stream);
 

@@ -672,21 +672,23 @@ int recap_copy_rows_2d(void* dst, int64_t dst_pitch, const void* src, int64_t sr
 int recap_scatter_rows(const void* src, int banks, int S, int D, void* const* out_ranks, int n_ranks,
                        int tokens_per_rank, int64_t out_bank_stride, int64_t out_row_stride, void* stream) {
   if (src == nullptr || out_ranks == nullptr || banks <= 0 || S <= 0 || (D != 64 && D != 128) ||
-      n_ranks < 1 || n_ranks > kMaxRanks || static_cast<int64_t>(n_ranks) * tokens_per_rank != S ||
-      out_bank_stride < 0 || out_row_stride < D)
+      n_ranks < 1 || n_ranks > kMaxRanks || tokens_per_rank <= 0 ||
+      static_cast<int64_t>(n_ranks) * tokens_per_rank != S || out_bank_stride < 0 || out_row_stride < D ||
+      out_bank_stride % 8 || out_row_stride % 8 || (reinterpret_cast<uintptr_t>(src) & 15))
     return kErrShape;
-  const size_t row = static_cast<size_t>(D) * 2;
+  ScatterArgs a{};
+  a.banks = banks;
+  a.S = S;
+  a.D = D;
+  a.tokens_per_rank = tokens_per_rank;
+  a.bank_stride = out_bank_stride;
+  a.row_stride = out_row_stride;
+  a.src = static_cast<const __nv_bfloat16*>(src);
   for (int q = 0; q < n_ranks; ++q) {
-    if (out_ranks[q] == nullptr) return kErrShape;
-    for (int b = 0; b < banks; ++b) {
-      const uint8_t* s = static_cast<const uint8_t*>(src) + (static_cast<size_t>(b) * S + static_cast<size_t>(q) * tokens_per_rank) * row;
-      uint8_t* d = static_cast<uint8_t*>(out_ranks[q]) + static_cast<size_t>(b) * out_bank_stride * 2;
-      if (cudaMemcpy2DAsync(d, static_cast<size_t>(out_row_stride) * 2, s, row, row, tokens_per_rank,
-                            cudaMemcpyDefault, static_cast<cudaStream_t>(stream)) != cudaSuccess)
-        return kErrLaunch;
-    }
+    if (out_ranks[q] == nullptr || (reinterpret_cast<uintptr_t>(out_ranks[q]) & 15)) return kErrShape;
+    a.dst[q] = static_cast<__nv_bfloat16*>(out_ranks[q]);
   }
-  return kOk;
+  return launch_scatter(a, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

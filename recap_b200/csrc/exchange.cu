@@ -36,7 +36,41 @@ __global__ void __launch_bounds__(256) push_kernel(const PushArgs a) {
   __threadfence_system();  // the stores are visible beyond this GPU before the kernel ends
 }
 
+// Rows of a locally computed [banks, S, D] output into the token shards of the ranks that
+// own them (bank b, token n -> dst[q] + b bank_stride + (n - q tokens_per_rank) row_stride).
+__global__ void __launch_bounds__(256) scatter_kernel(const ScatterArgs a) {
+  const int64_t cpr = a.D / 8;  // 16-byte chunks per row
+  const int64_t total = static_cast<int64_t>(a.banks) * a.S * cpr;
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < total;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = c / cpr;  // bank * S + token
+    const int64_t j = c - row * cpr;
+    const int64_t bank = row / a.S;
+    const int64_t n = row - bank * a.S;
+    const int q = static_cast<int>(n / a.tokens_per_rank);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.src) + c);
+    __nv_bfloat16* base = a.dst[0];
+#pragma unroll
+    for (int r = 1; r < kMaxRanks; ++r)
+      if (q == r) base = a.dst[r];
+    *reinterpret_cast<uint4*>(base + bank * a.bank_stride + (n - static_cast<int64_t>(q) * a.tokens_per_rank) * a.row_stride +
+                              j * 8) = v;
+  }
+  __threadfence_system();
+}
+
 }  // namespace
+
+int launch_scatter(const ScatterArgs& a, cudaStream_t s) {
+  const int64_t total = static_cast<int64_t>(a.banks) * a.S * (a.D / 8);
+  if (total <= 0) return kOk;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (total + 255) / 256;
+  const int grid = static_cast<int>(want < 8LL * sms ? want : 8LL * sms);
+  scatter_kernel<<<grid, 256, 0, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
 
 int launch_push(const PushArgs& a, cudaStream_t s) {
   const int64_t total = static_cast<int64_t>(a.tokens) * 3 * a.heads * a.D / 8;

@@ -60,6 +60,14 @@ struct PushArgs {
 };
 int launch_push(const PushArgs& a, cudaStream_t s);
 
+struct ScatterArgs {
+  int banks, S, D, tokens_per_rank;
+  int64_t bank_stride, row_stride;     // elements, in every destination
+  const __nv_bfloat16* src;            // [banks, S, D]
+  __nv_bfloat16* dst[kMaxRanks];       // token shard of each rank
+};
+int launch_scatter(const ScatterArgs& a, cudaStream_t s);
+
 // ------------------------------------------------------------------ C_vk on tensor cores
 struct CvkArgs {
   int banks, n_video, video_steps;  // video_steps = ceil(n_video / 64)
