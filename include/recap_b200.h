@@ -314,14 +314,6 @@ int recap_peer_close(void* ptr);
 int recap_push_heads(const void* src, int tokens, int heads, int D, int rank, int n_ranks,
                      void* const* recv_ranks, void* stream);
 
-/* `height` rows of `width` bytes from src (row pitch src_pitch bytes) to dst (dst_pitch), by a
- * copy engine (cudaMemcpy2DAsync; either side may be a peer buffer opened by recap_peer_import,
- * crossing NVLink as peer writes or reads).  The push form of the Ulysses exchange: each rank
- * writes its head groups' rows into the owners' receive buffers.  No counterpart in the
- * reference. */
-int recap_copy_rows_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
-                       int64_t height, void* stream);
-
 /* Store a [banks, S, D] bf16 output (contiguous, 16-byte aligned) into the ranks' token shards
  * as the *_ranks attention passes place it (one kernel of 16-byte peer stores over NVLink):
  * the step after a REFRESH whose dense output the refinement write reads locally.  Strides

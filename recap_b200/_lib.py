@@ -69,7 +69,6 @@ SIGNATURES: dict[str, tuple] = {
     "recap_peer_import": (_I, [_P, _P]),
     "recap_peer_close": (_I, [_P]),
     "recap_push_heads": (_I, [_P, _I, _I, _I, _I, _I, _P, _P]),
-    "recap_copy_rows_2d": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P]),
     "recap_scatter_rows": (_I, [_P, _I, _I, _I, _P, _I, _I, _I64, _I64, _P]),
     "recap_sparse_step": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "recap_refresh_partials": (_I, [_I, _I]),

@@ -658,17 +658,6 @@ int recap_push_heads(const void* src, int tokens, int heads, int D, int rank, in
   return launch_push(a, static_cast<cudaStream_t>(stream));
 }
 
-int recap_copy_rows_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
-                       int64_t height, void* stream) {
-  if (dst == nullptr || src == nullptr || width <= 0 || height <= 0 || dst_pitch < width || src_pitch < width)
-    return kErrShape;
-  return cudaMemcpy2DAsync(dst, static_cast<size_t>(dst_pitch), src, static_cast<size_t>(src_pitch),
-                           static_cast<size_t>(width), static_cast<size_t>(height), cudaMemcpyDefault,
-                           static_cast<cudaStream_t>(stream)) == cudaSuccess
-             ? kOk
-             : kErrLaunch;
-}
-
 int recap_scatter_rows(const void* src, int banks, int S, int D, void* const* out_ranks, int n_ranks,
                        int tokens_per_rank, int64_t out_bank_stride, int64_t out_row_stride, void* stream) {
   if (src == nullptr || out_ranks == nullptr || banks <= 0 || S <= 0 || (D != 64 && D != 128) ||
