@@ -27,7 +27,7 @@ so every rank takes the same decision the single-GPU operator would.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, fields
 
 import torch
 
@@ -79,18 +79,24 @@ def _bank_fits(bank: "DetailBank", sh) -> bool:
 
 @dataclass
 class DetailBank:
-    """One layer's cached refinement and its partition (recap/operator.py:33-59)."""
+    """What a layer keeps between a REFRESH and the SPARSE steps after it: the selected
+    key blocks and the cached correction of the tail.  The field names and dtypes are those
+    of recap/operator.py:33-59, which the host-bank streaming and the session read."""
 
-    partition: torch.Tensor | None = None  # [batch, heads, query blocks, key blocks] bool
-    # refinement of the tail output and of the tail log-mass
-    value: torch.Tensor | None = None  # [banks, rows, dim] fp16
-    log_mass: torch.Tensor | None = None  # [banks, rows] fp32
-    # coarse tail log-mass at the refresh, reference for the drift weight
-    coarse_lse: torch.Tensor | None = None  # [banks, rows] fp32
+    # selected key blocks per query block, [batch, heads, nB, nB] bool
+    partition: torch.Tensor | None = None
+    # the correction stored at the refresh: tail value ([banks, rows, dim] fp16) and tail
+    # log-mass ([banks, rows] fp32)
+    value: torch.Tensor | None = None
+    log_mass: torch.Tensor | None = None
+    # the coarse tail's log-mass at that refresh ([banks, rows] fp32): the drift weight of
+    # a later step compares the fresh coarse log-mass against it
+    coarse_lse: torch.Tensor | None = None
     valid: bool = False
     refreshed_at: int = 0
-    # error of the previous refinement, measured at this refresh
-    pending_stats: torch.Tensor | None = None  # [2] fp32: (sum sq error, sum sq output)
+    # (sum of squared error, sum of squared dense output) of the previous correction,
+    # scored at this refresh ([2] fp32), and that correction's age in steps
+    pending_stats: torch.Tensor | None = None
     pending_age: int | None = None
     sequence_tokens: int = 0
     n_video: int = 0
@@ -120,15 +126,9 @@ class DetailBank:
         self._mask = None
 
     def release(self) -> None:
-        self.partition = None
-        self._mask = None
-        self.value = None
-        self.log_mass = None
-        self.coarse_lse = None
-        self.valid = False
-        self.refreshed_at = 0
-        self.pending_stats = None
-        self.pending_age = None
+        """Back to the state of a bank that was never refreshed."""
+        for f in fields(self):
+            setattr(self, f.name, f.default)
 
 
 @dataclass
@@ -166,45 +166,45 @@ class Operator:
         n_streams: int = 1,
         process_group=None,
     ) -> "Operator":
-        """One sparse state per (stream, layer)."""
-        if n_layers < 1 or n_streams < 1:
+        """An operator with a ``SparseAttention`` state (basis of the sample) and a bank for
+        every layer of every guidance stream."""
+        if min(n_layers, n_streams) < 1:
             raise ValueError("n_layers and n_streams must be positive")
         if int(getattr(config, "block_size", 128)) != 128:
             raise ValueError("the exact block-sparse kernel requires block_size=128")
-        layers = [[SparseAttention(geometry, config) for _ in range(n_layers)] for _ in range(n_streams)]
-        return cls(config, geometry.layout, layers, process_group=process_group)
+        per_stream = lambda: [SparseAttention(geometry, config) for _ in range(n_layers)]  # noqa: E731
+        return cls(config, geometry.layout, [per_stream() for _ in range(n_streams)], process_group=process_group)
 
     @property
     def n_streams(self) -> int:
         return len(self.layers)
 
+    def _all_banks(self):
+        return (bank for row in self.banks for bank in row)
+
     def reset(self) -> None:
-        for row in self.banks:
-            for bank in row:
-                bank.release()
-        for row in self.layers:
-            for layer in row:
-                layer.reset()
-        self.kind = EXACT
-        self.step = 0
-        self.stream = 0
-        self.refreshed_layers = 0
+        """A new sample: every bank empty, every basis forgotten, the step counters at zero."""
+        for bank in self._all_banks():
+            bank.release()
+        for layer in (layer for row in self.layers for layer in row):
+            layer.reset()
+        self.kind, self.step, self.stream, self.refreshed_layers = EXACT, 0, 0, 0
 
     @property
     def banks_valid(self) -> bool:
-        """Whether every layer holds a refinement."""
-        return bool(self.banks) and all(bank.valid for row in self.banks for bank in row)
+        """True once every layer of every stream has stored a correction."""
+        banks = list(self._all_banks())
+        return bool(banks) and all(bank.valid for bank in banks)
 
     def begin_step(self, step: int, kind: str) -> None:
+        """Start a denoising step of the given kind; the calls that follow use it."""
         if kind not in (EXACT, REFRESH, SPARSE):
             raise ValueError(f"unknown computed call kind {kind!r}")
-        self.step = int(step)
-        self.kind = kind
-        self.stream = 0
-        self.refreshed_layers = 0
+        self.step, self.kind, self.stream, self.refreshed_layers = int(step), kind, 0, 0
 
     def set_stream(self, stream: int) -> None:
-        if not 0 <= stream < self.n_streams:
+        """Select the guidance stream whose banks the next calls use."""
+        if stream < 0 or stream >= self.n_streams:
             raise ValueError(f"stream {stream} outside 0..{self.n_streams - 1}")
         self.stream = int(stream)
 
@@ -457,31 +457,22 @@ class Operator:
     # -- the refinement error --------------------------------------------------------------
 
     def drain_validation(self) -> tuple[int, float] | None:
-        """Relative RMS error over all layers, and the smallest refinement age
-        (recap/operator.py:531-547)."""
-        stats: list[torch.Tensor] = []
-        ages: list[int] = []
-        for row in self.banks:
-            for bank in row:
-                if bank.pending_stats is not None and bank.pending_age is not None:
-                    stats.append(bank.pending_stats)
-                    ages.append(int(bank.pending_age))
-                bank.pending_stats = None
-                bank.pending_age = None
+        """Take the scores the last refreshes left: (youngest correction age, relative RMS
+        error sqrt(sum err^2 / sum ref^2) over every scored layer and rank), or None when no
+        layer was scored; the pending scores are cleared (recap/operator.py:531-547)."""
+        scored = [(b.pending_age, b.pending_stats) for b in self._all_banks()
+                  if b.pending_stats is not None and b.pending_age is not None]
+        for bank in self._all_banks():
+            bank.pending_stats, bank.pending_age = None, None
         self.check_device_status()
-        if not stats:
+        if not scored:
             return None
-        total = torch.stack(stats).sum(dim=0)
-        numerator, denominator = validation_reduce(total, self.process_group)
+        numerator, denominator = validation_reduce(torch.stack([st for _, st in scored]).sum(dim=0),
+                                                   self.process_group)
         error = math.sqrt(numerator / denominator) if denominator > 0.0 else float("inf")
-        return min(ages), error
+        return min(int(age) for age, _ in scored), error
 
     def peak_bank_bytes(self) -> int:
-        """Bytes held by the refinement."""
-        total = 0
-        for row in self.banks:
-            for bank in row:
-                for tensor in (bank.value, bank.log_mass):
-                    if tensor is not None:
-                        total += tensor.numel() * tensor.element_size()
-        return total
+        """Device or host bytes the stored corrections occupy (value and log-mass)."""
+        return sum(t.numel() * t.element_size() for b in self._all_banks() for t in (b.value, b.log_mass)
+                   if t is not None)
