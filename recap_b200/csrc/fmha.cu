@@ -41,6 +41,8 @@
 // the omitted blocks to the dense result.
 // Lists: A = [both keep | A only | B only | neither], B = [both | B only | A only |
 // neither], so the first and last parts share their K / V^T tiles.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -62,6 +64,11 @@ constexpr float kBoundSlack = 64.0f;
 // moving a quarter of them to the FP32 pipe makes the softmax the shorter of the two
 // (main loop 103 -> 95 clk per MMA on the bench workload; an eighth: 97, 3/8: 100).
 constexpr uint32_t kPolyPairs = 0x1111u;
+// The same for the blocks a REFRESH pass walks after a query block's kept ones: there
+// nearly every block takes the bounded path (no row maximum), which leaves the FP32 pipe
+// less room; a sixteenth measured best (REFRESH pass 143.2-143.6 ms against 147.5 with a
+// quarter, 144.5-146.2 with an eighth, 145.3-148.9 with none, 162+ with a half).
+constexpr uint32_t kPolyPairsOmitted = 0x0001u;
 
 template <int D>
 struct FmhaSmem {
@@ -663,25 +670,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float neg_m = -m_run;
       float sum[4] = {0.f, 0.f, 0.f, 0.f};
+      // exponentials, row sums and P of this block; kMask picks the pairs whose
+      // exponentials come from the FP32-pipe polynomial
+      auto exp_pass = [&](auto mask_tag) {
+        constexpr uint32_t kMask = decltype(mask_tag)::value;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float y0, y1;
-          fma2(y0, y1, s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1], scale_log2, scale_log2, neg_m, neg_m);
-          float p0, p1;
-          if ((kPolyPairs >> i) & 1u) {
-            exp2_poly2(p0, p1, y0, y1);
-          } else {
-            p0 = fast_exp2(y0);
-            p1 = fast_exp2(y1);
+          for (int i = 0; i < 16; ++i) {
+            float y0, y1;
+            fma2(y0, y1, s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1], scale_log2, scale_log2, neg_m, neg_m);
+            float p0, p1;
+            if ((kMask >> i) & 1u) {
+              exp2_poly2(p0, p1, y0, y1);
+            } else {
+              p0 = fast_exp2(y0);
+              p1 = fast_exp2(y1);
+            }
+            add2(sum[(i & 1) * 2], sum[(i & 1) * 2 + 1], p0, p1);
+            pk[i] = pack_bf16(p0, p1);
           }
-          add2(sum[(i & 1) * 2], sum[(i & 1) * 2 + 1], p0, p1);
-          pk[i] = pack_bf16(p0, p1);
+          tmem_st16(t_sx + c * 16, pk);
         }
-        tmem_st16(t_sx + c * 16, pk);
-      }
+      };
+      // The REFRESH pass's omitted blocks (after the head is written) take their own split;
+      // the kept blocks keep the block-sparse pass's, so the head keeps its bits.
+      if (refresh && r >= head_round)
+        exp_pass(std::integral_constant<uint32_t, kPolyPairsOmitted>{});
+      else
+        exp_pass(std::integral_constant<uint32_t, kPolyPairs>{});
       // O holds P.V of blocks 0..r-1 complete (the commit of S(r) covers PV(r-1));
       // PV(r) is not issued before this warp's pfull arrival below.
       if (r > 0 && __any_sync(0xffffffffu, rescale)) {
