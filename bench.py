@@ -73,10 +73,10 @@ def parse():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default=WORKLOAD["name"],
                    help="BASELINE config 4 (default), 2 or 3")
     p.add_argument("--exchange", choices=["push", "p2p", "nccl"], default="push",
-                   help="stack workload, the Ulysses exchange: copy-engine peer writes of the projections into "
-                        "the owners' receive buffers and the attention epilogue storing rows into the owners' "
-                        "shards (push); the layout pass reading the ranks' projections in place over NVLink "
-                        "(p2p); or NCCL all_to_all_single around the call (nccl)")
+                   help="stack workload, the Ulysses exchange: a kernel of peer stores writing the projections "
+                        "into the owners' receive buffers and the attention epilogue storing rows into the "
+                        "owners' shards (push); the layout pass reading the ranks' projections in place over "
+                        "NVLink (p2p); or NCCL all_to_all_single around the call (nccl)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-copy-streams", type=int, default=3,
                    help="host-to-device copy streams of the e2e leg (the three inputs share them)")
@@ -85,6 +85,9 @@ def parse():
     p.add_argument("--profile-steps", type=int, default=3, help="extra steps with per-kernel CUDA events")
     p.add_argument("--heads", type=int, default=None,
                    help="run only this many of the layer's heads (small cases for ncu captures)")
+    p.add_argument("--kernel", choices=["select"], default=None,
+                   help="time one kernel alone at the workload's shape instead of the layer call (select: "
+                        "recap_pool_select on seeded pooled means, about 45 MB on the device)")
     return p.parse_args()
 
 
@@ -907,6 +910,48 @@ def run_stack(args, w: dict, world: int, rank: int, dev, group) -> None:
 # ----------------------------------------------------------------------------- reference arm
 
 
+def run_kernel_select(args) -> None:
+    """``--kernel select``: the block selection (fp32 scores of every query-block x key-block
+    pair of every bank and the exact top-k) alone, at the workload's banks, block count, head
+    dimension and keep, on seeded pooled means (a shared low-rank part plus noise, so the
+    scores of a row lie close together as they do for smooth video).  A small case for ncu:
+    the means and the partition take about 45 MB at the default workload."""
+    from recap_b200 import _lib as lib
+
+    w = WORKLOADS[args.workload]
+    dev = torch.device("cuda", 0)
+    nv = w["grid"][0] * w["grid"][1] * w["grid"][2]
+    d = w["dim"]
+    banks = (args.heads or w["heads"]) * w["batch"]
+    nb = (nv + 127) // 128
+    keep = max(1, round(w["density"] * nb))
+    g = torch.Generator().manual_seed(0)
+    shared = torch.randn(nb, 16, generator=g) @ torch.randn(16, d, generator=g) / 4
+    qm = (shared + 0.5 * torch.randn(banks, nb, d, generator=g)).to(dev)
+    km = (shared + 0.5 * torch.randn(banks, nb, d, generator=g)).to(dev)
+    part = torch.empty(banks, nb, nb, dtype=torch.bool, device=dev)
+    st = lib.stream_handle(dev)
+
+    def run():
+        lib.call("recap_pool_select", lib.ptr(qm), lib.ptr(km), banks, nb, d, keep, 1 / math.sqrt(d), nv, 128,
+                 lib.ptr(part), st)
+
+    for _ in range(max(1, args.warmup)):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"kernel": "recap_pool_select", "ms": round(ms, 4), "steps": args.steps,
+                      "config": {"workload": w["name"], "banks": banks, "key_blocks": nb, "head_dim": d,
+                                 "keep": keep, "data": "seeded synthetic pooled means"},
+                      "kept_per_row": round(float(part.sum(-1).float().mean()), 2)}), flush=True)
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -930,5 +975,7 @@ if __name__ == "__main__":
     a = parse()
     if a.impl == "reference":
         run_reference(a)
+    elif a.kernel == "select":
+        run_kernel_select(a)
     else:
         run_ours(a)

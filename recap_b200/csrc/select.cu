@@ -10,54 +10,108 @@
 // overlap_kernel  |new & old| and |new| of two partitions (recap/operator.py:288-291, 425-428).
 // mask_kernel     build_kernel_block_mask (recap/kernels/block_sparse.py:52-75).
 // center_kernel   _drift_center (recap/operator.py:148-150) from per-query-block partial sums.
+#include "common.cuh"
 #include "kernels.h"
 
 namespace recap {
 namespace {
 
-constexpr int kRows = 8;  // query blocks per CTA (one warp each in the top-k phase)
+constexpr int kRows = 16;        // query blocks per CTA (one warp each in the top-k phase)
+constexpr int kSelThreads = 512;
+constexpr int kDc = 8;           // dimensions of every key mean staged per step
+constexpr int kPitch = kDc + 1;  // odd row pitch: lane l reads word 9 l + dd, no bank conflicts
 
 __device__ __forceinline__ uint32_t order_key(float x) {
   const uint32_t u = __float_as_uint(x);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-template <int D>
-__global__ void __launch_bounds__(256) select_kernel(const SelectArgs a) {
+__device__ __forceinline__ void cp_async4(uint32_t dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// Scores: each thread holds KPT key blocks x the CTA's 16 query blocks in registers.  The key
+// means go through shared memory 8 dimensions at a time (32-byte row segments, whole sectors;
+// a lane per key row reading its own 512-byte row had touched 32 lines per load), by
+// asynchronous copies into two buffers, so one chunk is in flight while the other is used.
+// Every score is still one fmaf chain over d = 0 .. D-1: the order of the fp32 sums is that
+// of the plain dot product.
+template <int D, int KPT>
+__global__ void __launch_bounds__(kSelThreads, KPT <= 2 ? 2 : 1) select_kernel(const SelectArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  float* qm = reinterpret_cast<float*>(smem);                 // [kRows][D]
-  uint32_t* keys = reinterpret_cast<uint32_t*>(qm + kRows * D);  // [kRows][nB]
-  uint32_t* hist = keys + kRows * a.nB;                       // [8 warps][256]
+  const int nB = a.nB;
+  float* qt = reinterpret_cast<float*>(smem);                    // [D][kRows]: q means, transposed
+  uint32_t* hist = reinterpret_cast<uint32_t*>(qt + D * kRows);  // [kRows warps][256]
+  float* kc = reinterpret_cast<float*>(hist + kRows * 256);      // 2 x [nB][kPitch] while scoring
+  uint32_t* keys = reinterpret_cast<uint32_t*>(kc);              // [kRows][nB] afterwards
   const int bank = blockIdx.y;
   const int i0 = blockIdx.x * kRows;
-  const int nB = a.nB;
   const int tid = threadIdx.x;
-  for (int idx = tid; idx < kRows * D; idx += 256) {
+  for (int idx = tid; idx < kRows * D; idx += kSelThreads) {
     const int r = idx / D;
+    const int d = idx - r * D;
     const int i = i0 + r;
-    qm[idx] = i < nB ? a.qmean[(static_cast<size_t>(bank) * nB + i) * D + (idx % D)] : 0.f;
+    qt[d * kRows + r] = i < nB ? a.qmean[(static_cast<size_t>(bank) * nB + i) * D + d] : 0.f;
   }
-  __syncthreads();
+  float acc[KPT][kRows];
+#pragma unroll
+  for (int m = 0; m < KPT; ++m)
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) acc[m][r] = 0.f;
   const float* kbase = a.kmean + static_cast<size_t>(bank) * nB * D;
-  for (int j = tid; j < nB; j += 256) {
-    float acc[kRows];
+  const uint32_t kc_u32 = static_cast<uint32_t>(__cvta_generic_to_shared(kc));
+  const int buf_words = nB * kPitch;
+  auto stage = [&](int chunk) {  // dimensions 8 chunk .. 8 chunk + 7 of every key mean
+    const uint32_t dst0 = kc_u32 + static_cast<uint32_t>((chunk & 1) * buf_words) * 4u;
+    for (int idx = tid; idx < nB * kDc; idx += kSelThreads) {
+      const int j = idx / kDc;
+      const int e = idx - j * kDc;
+      cp_async4(dst0 + static_cast<uint32_t>(j * kPitch + e) * 4u, kbase + static_cast<size_t>(j) * D + chunk * kDc + e);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  constexpr int kChunks = D / kDc;
+  stage(0);
+  for (int c = 0; c < kChunks; ++c) {
+    if (c + 1 < kChunks) {
+      stage(c + 1);  // its buffer was last read in step c - 1, which ended at a barrier
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // chunk c has landed for every thread (and, the first time, qt is written)
+    const float* kb = kc + (c & 1) * buf_words;
+#pragma unroll 1
+    for (int dd = 0; dd < kDc; ++dd) {
+      float kv[KPT];
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
-    const float4* krow = reinterpret_cast<const float4*>(kbase + static_cast<size_t>(j) * D);
-#pragma unroll 4
-    for (int c = 0; c < D / 4; ++c) {
-      const float4 kv = krow[c];
+      for (int m = 0; m < KPT; ++m) {
+        const int j = tid + m * kSelThreads;
+        kv[m] = j < nB ? kb[j * kPitch + dd] : 0.f;
+      }
+      const float4* q4 = reinterpret_cast<const float4*>(qt + (c * kDc + dd) * kRows);
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) {
-        const float4 qv = *reinterpret_cast<const float4*>(qm + r * D + 4 * c);
-        acc[r] = fmaf(qv.x, kv.x, acc[r]);
-        acc[r] = fmaf(qv.y, kv.y, acc[r]);
-        acc[r] = fmaf(qv.z, kv.z, acc[r]);
-        acc[r] = fmaf(qv.w, kv.w, acc[r]);
+      for (int r4 = 0; r4 < kRows / 4; ++r4) {
+        const float4 q = q4[r4];
+#pragma unroll
+        for (int m = 0; m < KPT; ++m) {  // two rows per packed fma (each lane an fp32 fma, same bits)
+          fma2(acc[m][4 * r4 + 0], acc[m][4 * r4 + 1], q.x, q.y, kv[m], kv[m], acc[m][4 * r4 + 0],
+               acc[m][4 * r4 + 1]);
+          fma2(acc[m][4 * r4 + 2], acc[m][4 * r4 + 3], q.z, q.w, kv[m], kv[m], acc[m][4 * r4 + 2],
+               acc[m][4 * r4 + 3]);
+        }
       }
     }
+    __syncthreads();  // every thread is done with buffer c & 1 before step c + 1 refills it
+  }
+  __syncthreads();  // the last chunk is consumed: its space takes the order keys
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) keys[r * nB + j] = order_key(acc[r] * a.scale);
+  for (int m = 0; m < KPT; ++m) {
+    const int j = tid + m * kSelThreads;
+    if (j < nB) {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) keys[r * nB + j] = order_key(acc[m][r] * a.scale);
+    }
   }
   __syncthreads();
 
@@ -197,21 +251,31 @@ __global__ void center_kernel(const CenterArgs a) {
 
 }  // namespace
 
-int launch_select(const SelectArgs& a, cudaStream_t s) {
-  if (a.nB <= 0 || a.banks <= 0) return kErrShape;
-  const size_t smem = static_cast<size_t>(kRows) * a.D * 4 + static_cast<size_t>(kRows) * a.nB * 4 + 8 * 256 * 4;
-  if (smem > 220 * 1024) return kErrShape;
+template <int D, int KPT>
+int launch_select_t(const SelectArgs& a, size_t smem, cudaStream_t s) {
+  cudaFuncSetAttribute(select_kernel<D, KPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   dim3 grid((a.nB + kRows - 1) / kRows, a.banks);
-  if (a.D == 128) {
-    cudaFuncSetAttribute(select_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    select_kernel<128><<<grid, 256, smem, s>>>(a);
-  } else if (a.D == 64) {
-    cudaFuncSetAttribute(select_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    select_kernel<64><<<grid, 256, smem, s>>>(a);
-  } else {
-    return kErrShape;
-  }
+  select_kernel<D, KPT><<<grid, kSelThreads, smem, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+template <int D>
+int launch_select_d(const SelectArgs& a, size_t smem, cudaStream_t s) {
+  if (a.nB <= kSelThreads) return launch_select_t<D, 1>(a, smem, s);
+  if (a.nB <= 2 * kSelThreads) return launch_select_t<D, 2>(a, smem, s);
+  return launch_select_t<D, 4>(a, smem, s);
+}
+
+int launch_select(const SelectArgs& a, cudaStream_t s) {
+  if (a.nB <= 0 || a.banks <= 0 || a.nB > 4 * kSelThreads) return kErrShape;
+  // q means + histograms + max(two key-mean chunks, order keys)
+  const size_t chunk = 2 * static_cast<size_t>(a.nB) * kPitch * 4;
+  const size_t keys = static_cast<size_t>(kRows) * a.nB * 4;
+  const size_t smem = static_cast<size_t>(a.D) * kRows * 4 + kRows * 256 * 4 + (chunk > keys ? chunk : keys);
+  if (smem > 220 * 1024) return kErrShape;
+  if (a.D == 128) return launch_select_d<128>(a, smem, s);
+  if (a.D == 64) return launch_select_d<64>(a, smem, s);
+  return kErrShape;
 }
 
 int launch_overlap(const OverlapArgs& a, cudaStream_t s) {

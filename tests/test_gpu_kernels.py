@@ -90,7 +90,7 @@ def _selection_matches(got: torch.Tensor, scores: torch.Tensor, keep: int, force
 
 
 @pytest.mark.parametrize("d", [64, 128])
-@pytest.mark.parametrize("nv,keep", [(2048, 4), (700, 2), (118800 // 16, 46)])
+@pytest.mark.parametrize("nv,keep", [(2048, 4), (700, 2), (118800 // 16, 46), (1400 * 128 - 5, 140)])
 def test_pool_select_topk(d, nv, keep):
     from recap_b200 import _lib as lib
 
