@@ -41,15 +41,21 @@ REFRESH = "refresh"
 SPARSE = "sparse"
 
 
-def layer_counts_reduce(counts: torch.Tensor, group=None) -> tuple[int, int]:
-    """Sum the (kept, total) overlap counts of this rank's heads over the process group:
-    the reference takes the re-selection decision over the whole layer
-    (recap/operator.py:282-291, 425-428), and with head sharding the layer spans ranks."""
+def layer_counts_sum(counts: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum the (kept, total) overlap counts of this rank's heads over the process group, in
+    place and without a host read: the reference takes the re-selection decision over the
+    whole layer (recap/operator.py:282-291, 425-428), and with head sharding the layer
+    spans ranks."""
     if group is not None:
         import torch.distributed as dist
 
         dist.all_reduce(counts, group=group)
-    kept, total = (int(x) for x in counts.cpu())
+    return counts
+
+
+def layer_counts_reduce(counts: torch.Tensor, group=None) -> tuple[int, int]:
+    """``layer_counts_sum`` and the host read of the two sums."""
+    kept, total = (int(x) for x in layer_counts_sum(counts, group).cpu())
     return kept, total
 
 
@@ -334,14 +340,15 @@ class Operator:
 
     # -- refresh ---------------------------------------------------------------------------
 
-    def _layer_overlap(self, new: torch.Tensor, old: torch.Tensor) -> tuple[int, int]:
-        """(kept, total) = (|new & old|, |new|) over the whole layer (all ranks)."""
+    def _layer_overlap(self, new: torch.Tensor, old: torch.Tensor) -> torch.Tensor:
+        """Device int64 (kept, total) = (|new & old|, |new|) over the whole layer (all ranks),
+        queued on the stream; the caller reads it on the host when it needs the decision."""
         counts = torch.empty(2, dtype=torch.int64, device=new.device)
         self.launches.run(
             "recap_partition_overlap", 1, _lib.ptr(new), _lib.ptr(old), new.numel(), _lib.ptr(counts),
             _lib.stream_handle(new.device),
         )
-        return layer_counts_reduce(counts, self.process_group)
+        return layer_counts_sum(counts, self.process_group)
 
     @torch.no_grad()
     def _refresh(self, layer: SparseAttention, bank: DetailBank, query, key, value, io=None) -> torch.Tensor:
@@ -349,9 +356,10 @@ class Operator:
         (recap/operator.py:331-473).
 
         The re-selection test of a revalidating refresh (recap/operator.py:420-435) depends
-        only on the block means of Q and K, so it runs first: the new selection and its
-        layer-wide overlap with the old partition decide, before any attention, which
-        partition the new refinement is stored under.  The old partition's head and coarse
+        only on the block means of Q and K, so it is queued first: the new selection and its
+        layer-wide overlap with the old partition decide which partition the new refinement
+        is stored under (the host reads the overlap once the passes that use the old partition
+        either way are queued, so the GPU never waits for it).  The old partition's head and coarse
         tail score the old refinement and, when the partition is kept, also give the new
         one, so one pass over every key block yields the dense output and that head.  Only
         a re-selection needs a second head pass, under the new partition."""
@@ -368,11 +376,12 @@ class Operator:
             bank.release()
         revalidating = bank.valid
         selection = layer.head_partition(inputs, scale)
-        reselect = False
+        overlap = None
         if revalidating:
-            # keep the old partition if the selection barely changed over the whole layer
-            kept, total = self._layer_overlap(selection, bank.partition)
-            reselect = not keep_partition(kept, total, self.config.rerank_min_overlap)
+            # the new selection's overlap with the old partition, over the whole layer; the
+            # passes below use the old partition either way, so the host reads the counts only
+            # after they are queued (the GPU does not wait for the host's decision)
+            overlap = self._layer_overlap(selection, bank.partition)
         else:
             bank.set_partition(selection, sh.S, sh.n_video)
         full_out, full_lse, head_o, head_lse = self._dense_and_head(inputs, bank.partition, scale, status)
@@ -390,6 +399,11 @@ class Operator:
         if stats is not None:
             bank.pending_stats = stats
             bank.pending_age = self.step - bank.refreshed_at
+        reselect = False
+        if overlap is not None:
+            # keep the old partition if the selection barely changed over the whole layer
+            kept, total = (int(x) for x in overlap.cpu())
+            reselect = not keep_partition(kept, total, self.config.rerank_min_overlap)
         if reselect:
             bank.set_partition(selection, sh.S, sh.n_video)
             del head_o, head_lse, coarse, coarse_lse
