@@ -112,6 +112,7 @@ int recap_value_key_covariance(const void* v_transposed, const void* k_centred_t
  * block_proxy_mask (recap/sparse/router.py:10-23): score = (qbar . kbar) * scale in fp32,
  * the `keep` highest-scoring key blocks per query block (ties: lower block index first),
  * then the trailing partial video block selected as a row and a column.
+ * nB must not exceed 2048 (the attention kernels' limit); larger calls return RECAP_ERR_SHAPE.
  *   partition      [banks, nB, nB] uint8 (bool) out */
 int recap_pool_select(const float* q_mean, const float* k_mean, int banks, int nB, int D, int keep,
                       float scale, int n_video, int block_size, uint8_t* partition, void* stream);
