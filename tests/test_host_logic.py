@@ -95,6 +95,9 @@ def test_library_rejects_bad_shapes_without_a_gpu():
     lib = _lib.load()
     # D must be 64 or 128: rejected on the host before any device call
     assert lib.recap_pool_select(None, None, 1, 4, 96, 1, 1.0, 512, 128, None, None) == _lib.RECAP_ERR_SHAPE
+    # more key blocks than the attention kernels take (2048)
+    assert lib.recap_pool_select(None, None, 1, 2049, 128, 1, 1.0, 2049 * 128, 128, None, None) == \
+        _lib.RECAP_ERR_SHAPE
     assert lib.recap_closure_workspace_floats(2, 64, 2048) == 2 * 2 * 1 * 64 * 64
 
 
