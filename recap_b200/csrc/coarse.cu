@@ -571,6 +571,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       // alpha = 1 and an unchanged max, so the two give the same bits.
       const bool bounded =
           m_run != -INFINITY && __all_sync(0xffffffffu, qn_l2 * tile_kn[j] + bound_add <= m_run + kBoundSlack);
+      if (bounded && j * kTileN + h * kHalf >= nB) {
+        // Every column of this half is padding past the last block mean (column term -inf):
+        // its exponentials are 0 (2^-125 on the polynomial pairs, below the last bit of any
+        // row sum) and the padded v_bar rows are 0, so the half writes P = 0, takes part in
+        // the tile's two barriers and leaves the issue slots to the other half.
+        uint32_t zero[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) zero[i] = 0u;
+#pragma unroll
+        for (int c = 0; c < kHalf / 32; ++c) tmem_st16(t_s1 + b * kTileN + h * kHalf + c * 16 + lane_base, zero);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bars.s2free);  // this half reads no S2 column of the tile
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bars.pfull + b);
+        continue;
+      }
       if (bounded) {
         static_assert(kHalf / 16 >= 2, "S2 is released after the second-to-last step's loads");
         const float neg_m = -m_run;
